@@ -1,0 +1,416 @@
+"""Benchmark: the 40-layer Q4_K/Q6_K expert stack decode step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch T] [--impl ours|reference]
+
+Workload: 40 layers x (256 routed + 1 shared) experts, all
+resident in HBM (20.97 GB of Q4_K gate/up and Q6_K down blocks, synthetic from a
+seed with the benchmark value distributions), hidden 2048, expert inter 512,
+top-8 softmax routing over an fp32 256 x 2048 router.  One step decodes T
+tokens through all 40 MoE layers; each layer's input is the RMS-normalised
+residual stream left by the previous layer (h <- h + moe_l(rmsnorm(h))), so
+every layer waits for the previous layer's combine, as decode does.  With N
+GPUs the experts are split expert-parallel (rank r holds experts
+[r*256/N, (r+1)*256/N)) and each layer's partial outputs are combined over
+NVLink.  Inputs cycle through 16 distinct seeded hidden states so routing
+changes between steps; one step streams ~0.8 GB (T=1) to ~18 GB (T=64) of
+distinct expert weights, far more than the 126 MB L2, so no flush is needed.
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q4_K/Q6_K expert matvec HBM GB/s (% of peak); MoE-stack decode tok/s at 1/2/4/8 B200"
+H, I, E, K_TOP, LAYERS = 2048, 512, 256, 8, 40
+GATE_B = I * H // 256 * 144      # one expert's gate (= up) matrix, bytes
+DOWN_B = H * I // 256 * 210      # one expert's down matrix, bytes
+EXPERT_B = 2 * GATE_B + DOWN_B   # 2,039,808
+N_INPUTS = 16
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def layer_bytes(groups: int, pairs: int, T: int) -> dict:
+    """Algorithmic bytes of one layer's three kernels (each weight byte once)."""
+    k1 = E * H * 4 + H * 2 + T * H * 4 + T * H * 2 + T * (H // 32) * 4 + T * E * 4
+    k2 = groups * 2 * GATE_B + T * H * 2 + pairs * I * 2
+    k3 = groups * DOWN_B + pairs * I * 2 + 2 * T * H * 4
+    return {"route": k1, "gateup": k2, "down": k3}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200", "-f", self.path],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 9:
+                        rows.append(parts)
+            os.unlink(self.path)
+        except Exception:
+            return None
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        loaded = [s for s, p in zip(sm, pw) if p >= (max(pw) * 0.5 if pw else 0)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the reference's own CPU path (oracle/_ref) or the oracle port
+# ---------------------------------------------------------------------------
+class CpuLayerSampler:
+    """Runs whole MoE layers of the benchmark stack on the host with the
+    reference's CPU code: route_layer's arithmetic (one_layer.cu:937-992) and the
+    expert block of expert_bench.cu:158-179 (OpenMP over the top-k experts +
+    shared expert, cpu_tensor_matvec / cpu_swiglu, layer_ops.cu)."""
+
+    def __init__(self, seed: int, threads: int):
+        import numpy as np
+
+        import breadv2_b200 as bb
+        import oracle
+
+        self.np, self.bb, self.oracle = np, bb, oracle
+        self.kind = "reference" if oracle.ref_available() else "port"
+        self.seed, self.threads = seed, threads
+        self.cache = {}
+
+    def _sid(self, layer, kind, e):
+        return (layer << 32) | (kind << 24) | e
+
+    def _blocks(self, layer, kind, e, n, qt):
+        key = (layer, kind, e)
+        if key not in self.cache:
+            self.cache[key] = self.bb.synth_blocks_host(n, qt, self.seed, self._sid(layer, kind, e))
+        return self.cache[key]
+
+    def layer_inputs(self, layer):
+        bb = self.bb
+        W = bb.synth_normal_host(E * H, 0.02, self.seed, self._sid(layer, 6, 0)).reshape(E, H)
+        sg = bb.synth_normal_host(H, 0.02, self.seed, self._sid(layer, 7, 0), half=True)
+        return W, sg
+
+    def run_layer(self, layer, h, W, sg):
+        """One layer for T tokens: returns seconds spent in the reference code."""
+        np, o = self.np, self.oracle
+        x = (h / np.sqrt((h.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + 1e-6)).astype(np.float32)
+        t0 = time.perf_counter()
+        if self.kind == "reference":
+            idx, wt, sgw = o.ref_route(x, W, sg, K_TOP)
+        else:
+            idx, wt, sgw, _ = o.route(x, W, sg, K_TOP)
+        t1 = time.perf_counter()
+        nb_g, nb_d = I * H // 256, H * I // 256
+        empty = np.zeros(1, np.uint8)
+        gate, up, down = [empty] * E, [empty] * E, [empty] * E
+        for e in set(idx.ravel().tolist()):
+            gate[e] = self._blocks(layer, 0, e, nb_g, 12)
+            up[e] = self._blocks(layer, 1, e, nb_g, 12)
+            down[e] = self._blocks(layer, 2, e, nb_d, 14)
+        sh = (self._blocks(layer, 3, 0, nb_g, 12), self._blocks(layer, 4, 0, nb_g, 12),
+              self._blocks(layer, 5, 0, nb_d, 14))
+        es = o.ExpertSet(gate, up, down, *sh)
+        t2 = time.perf_counter()
+        if self.kind == "reference":
+            out = o.ref_moe_block(es, x, idx, wt, sgw, H, I, self.threads)
+        else:
+            out = o.moe_f32(es, x, idx, wt, sgw, H, I)
+        t3 = time.perf_counter()
+        return (t1 - t0) + (t3 - t2), h + out
+
+
+def cpu_sample(T: int, seed: int, threads: int, budget_s: float = 15.0):
+    """Time whole reference-CPU layers until ~budget_s of CPU work; returns
+    (tok/s for the 40-layer stack, layers timed, kind)."""
+    import numpy as np
+
+    import breadv2_b200 as bb
+
+    s = CpuLayerSampler(seed, threads)
+    h = bb.synth_normal_host(T * H, 1.0, seed, 777).reshape(T, H)
+    spent, layers = 0.0, 0
+    while layers < LAYERS and (layers == 0 or spent < budget_s):
+        W, sg = s.layer_inputs(layers)
+        dt, h = s.run_layer(layers, h, W, sg)
+        spent += dt
+        layers += 1
+    per_layer = spent / layers
+    return T / (per_layer * LAYERS), layers, s.kind, per_layer
+
+
+def run_reference(args, rank: int, world: int) -> int:
+    """--impl reference: the reference's CPU implementation of the path on the
+    host cores, same metric and config; rank 0 only."""
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    import breadv2_b200 as bb
+
+    threads = os.cpu_count() or 1
+    s = CpuLayerSampler(args.seed, threads)
+    T = args.batch
+    hs = [bb.synth_normal_host(T * H, 1.0, args.seed, 900 + i).reshape(T, H) for i in range(N_INPUTS)]
+    times = []
+    for i in range(args.warmup + args.steps):
+        layer = i % LAYERS
+        W, sg = s.layer_inputs(layer)
+        dt, _ = s.run_layer(layer, hs[i % N_INPUTS], W, sg)
+        if i >= args.warmup:
+            times.append(dt)
+    per_layer = sum(times) / len(times)
+    value = T / (per_layer * LAYERS)
+    sample = f"{args.steps} timed layers (one MoE layer per step, cycling layers 0..39) at T={T}; tok/s = T / (40 x mean layer time)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * LAYERS * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_block(args, world),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": s.kind, "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_block(args, world):
+    return {"workload": "config 5: 40-layer Q4_K/Q6_K expert stack, 40 x (256 routed + 1 shared) experts resident "
+                        "(20.97 GB), decode step of `batch` tokens",
+            "layers": LAYERS, "hidden": H, "inter": I, "experts": E, "top_k": K_TOP, "shared_expert": True,
+            "batch": args.batch, "global_batch": args.batch, "layer_input": "rmsnorm(residual), layers chained",
+            "parallelism": f"ep{world}", "l2": "inputs larger than L2 (>= 0.8 GB of distinct weights per step)"}
+
+
+# ---------------------------------------------------------------------------
+# GPU: this library
+# ---------------------------------------------------------------------------
+def run_ours(args, rank: int, world: int, local_rank: int) -> int:
+    import numpy as np
+    import torch
+
+    import breadv2_b200 as bb
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    T = args.batch
+    st = bb.ExpertStack(n_layers=LAYERS, hidden=H, inter=I, n_experts=E, top_k=K_TOP, max_tokens=T,
+                        shared_expert=True, norm_eps=1e-6, seed=args.seed, rank=rank, world=world)
+    if world > 1:
+        st.connect_peers(dist)
+    stream = torch.cuda.current_stream()
+    inputs = [bb.synth_normal(T * H, 1.0, args.seed, 900 + i, device=dev).view(T, H) for i in range(N_INPUTS)]
+    h = torch.empty(T, H, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def one(i):
+        h.copy_(inputs[i % N_INPUTS])
+        st.step(h)
+
+    for i in range(args.warmup):
+        one(i)
+    torch.cuda.synchronize()
+    assert bb.device_error() == 0, "device-side wait timed out"
+
+    clocks = ClockSampler(local_rank)
+    if not args.quick:
+        clocks.start()
+    # keep the GPU loaded ~1 s before timing so the clock samples see steady state
+    t_end = time.time() + (0.0 if args.quick else 1.0)
+    i = 0
+    while time.time() < t_end:
+        one(i)
+        i += 1
+        if i % 8 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        one(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if args.quick:
+        if rank == 0:
+            print(json.dumps({"quick": True, "ms_per_step": ms / args.steps, "batch": T, "n_gpus": world}), flush=True)
+        st.close()
+        if dist is not None:
+            dist.destroy_process_group()
+        return 0
+
+    # end to end through the host-buffer entry point (H2D + step + D2H per step)
+    hin = [x.cpu().pin_memory() for x in inputs]
+    hout = torch.empty(T, H, dtype=torch.float32).pin_memory()
+    for i in range(2):
+        st.step_host(hin[i], hout)
+    torch.cuda.synchronize()
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for i in range(args.steps):
+        st.step_host(hin[i % N_INPUTS], hout)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = e2.elapsed_time(e3)
+    clk = clocks.stop()
+
+    # per-kernel durations (instrumented replay of the same step) and routing stats
+    h.copy_(inputs[0])
+    kms = st.profile_step(h)
+    groups, pairs = st.routing_stats()
+    assert bb.device_error() == 0, "device-side wait timed out"
+
+    if dist is not None:
+        t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_e2e = float(t[0]), float(t[1])
+    if rank != 0:
+        st.close()
+        dist.destroy_process_group()
+        return 0
+
+    hbm_peak, peak_kind = peaks()
+    ms_step = ms / args.steps
+    value = T / (ms_step * 1e-3)
+    bytes_per_layer = [layer_bytes(int(g), int(p), T) for g, p in zip(groups, pairs)]
+    names = ["route", "gateup", "down"]
+    tot_ms = {n: float(kms[:, j].sum()) for j, n in enumerate(names)}
+    tot_b = {n: float(sum(b[n] for b in bytes_per_layer)) for n in names}
+    dom = max(names, key=lambda n: tot_ms[n])
+    achieved = tot_b[dom] / (tot_ms[dom] * 1e-3) / 1e9
+    kernel_names = {"route": "moe_route_kernel", "gateup": "moe_gateup_kernel<8>", "down": "moe_down_kernel<2>"}
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tfile):
+        try:
+            tj = json.load(open(tfile))
+            traffic = tj.get(f"{kernel_names[dom]}@T{T}")
+        except Exception:
+            traffic = None
+    step_bytes = sum(sum(b.values()) for b in bytes_per_layer)
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        threads = min(8, os.cpu_count() or 1)
+        v, layers, kind, per_layer = cpu_sample(T, args.seed, threads)
+        cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": kind,
+               "sample": f"{layers} of 40 MoE layers at T={T} on the host ({per_layer * 1e3:.1f} ms/layer, "
+                         f"OpenMP over experts as expert_bench.cu:158-179); tok/s = T / (40 x layer time)"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "i32+f32", "data": "synthetic",
+        "config": config_block(args, world),
+        "roofline": {"bound": "hbm", "kernel": kernel_names[dom], "achieved": achieved, "peak": hbm_peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": tot_b[dom] / LAYERS,
+                     "avg_launch_us": tot_ms[dom] / LAYERS * 1e3},
+        "kernels_us_per_layer": {n: tot_ms[n] / LAYERS * 1e3 for n in names},
+        "step_hbm_gbs": step_bytes / (ms_step * 1e-3) / 1e9,
+        "experts_per_layer": float(np.mean(groups)),
+        "cpu_baseline": cpu,
+        "e2e": {"value": T / (ms_e2e / args.steps * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": T * H * 4,
+                "d2h_bytes_per_step": T * H * 4},
+        "gpu_launches": args.steps * st.launches_per_step(T),
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    st.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1, help="tokens per decode step (T)")
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true",
+                    help="profiler runs: timed steps only (no load phase, end-to-end pass, kernel events or CPU baseline)")
+    args = ap.parse_args(argv)
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and "WORLD_SIZE" in os.environ:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,247 @@
+"""breadv2_b200 -- sm_100a quantised-expert MoE path of the BREAD decode engine.
+
+Host-side mirror of the reference's operator interface for this path, over the
+C ABI of ``include/bread_b200.h`` (``libbread_b200.so``).  Device memory and
+streams come from PyTorch; every computation runs in the CUDA library.
+
+Reference interfaces mirrored (arahe-dev/breadv2):
+  matvec            bread_matvec                kernels.cu:289-308
+  rmsnorm_half ...  bread_rmsnorm_half etc.     layer_logic.cu:28-31
+  moe_route         route_layer (on device)     one_layer.cu:937-992
+  moe_ffn           MoE block of one layer      one_layer.cu:1820-1985
+  ExpertStack       decode loop over layers     main.cu:677-713 (MoE part)
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._lib import BreadError, StackConfig, check, device_error, last_error, lib  # noqa: F401
+
+QTYPE_Q8_0, QTYPE_Q4_K, QTYPE_Q6_K = 8, 12, 14
+BLOCK_BYTES = {QTYPE_Q4_K: 144, QTYPE_Q6_K: 210, QTYPE_Q8_0: 34}
+BLOCK_ELEMS = {QTYPE_Q4_K: 256, QTYPE_Q6_K: 256, QTYPE_Q8_0: 32}
+
+
+def _s(stream) -> ctypes.c_void_p:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+def _p(t) -> ctypes.c_void_p:
+    if t is None:
+        return ctypes.c_void_p(0)
+    if isinstance(t, int):
+        return ctypes.c_void_p(t)
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def matrix_bytes(rows: int, cols: int, qtype: int) -> int:
+    return rows * (cols // BLOCK_ELEMS[qtype]) * BLOCK_BYTES[qtype]
+
+
+# ---- GEMV ----------------------------------------------------------------
+def matvec(w, x, y, rows: int, cols: int, qtype: int, stream=None) -> None:
+    """bread_matvec (kernels.cu:289): fp16 x [cols] -> fp16 y [rows]."""
+    check(lib().bread_matvec_f16(_p(w), _p(x), _p(y), rows, cols, qtype, _s(stream)), "bread_matvec")
+
+
+def matvec_f32(w, x, rows: int, cols: int, qtype: int, y=None, stream=None):
+    """fp32 y = W x.  x: [cols] or [T, cols] (T <= 64) fp32 on the device."""
+    T = 1 if x.dim() == 1 else x.shape[0]
+    if y is None:
+        y = torch.empty((rows,) if x.dim() == 1 else (T, rows), dtype=torch.float32, device=x.device)
+    if T == 1:
+        check(lib().bread_matvec_f32(_p(w), _p(x), _p(y), rows, cols, qtype, _s(stream)), "bread_matvec_f32")
+    else:
+        check(lib().bread_matvec_batch_f32(_p(w), _p(x), _p(y), rows, cols, qtype, T, _s(stream)),
+              "bread_matvec_batch_f32")
+    return y
+
+
+def dequant(w, n_blocks: int, qtype: int, out=None, stream=None):
+    """Bit-exact dequantisation (layer_ops.cu:44-105) of n_blocks blocks to fp32."""
+    if out is None:
+        out = torch.empty(n_blocks * BLOCK_ELEMS[qtype], dtype=torch.float32, device=w.device)
+    check(lib().bread_dequant(_p(w), _p(out), n_blocks, qtype, _s(stream)), "bread_dequant")
+    return out
+
+
+# ---- fp16 glue (layer_logic.cu:28-31) --------------------------------------
+def rmsnorm_half(x, w, eps: float, stream=None) -> None:
+    check(lib().bread_rmsnorm_half_c(_p(x), _p(w), x.numel(), eps, _s(stream)), "bread_rmsnorm_half")
+
+
+def silu_mul(gate, up, stream=None) -> None:
+    check(lib().bread_silu_mul_c(_p(gate), _p(up), gate.numel(), _s(stream)), "bread_silu_mul")
+
+
+def scale_accum(dst, src, scale: float, stream=None) -> None:
+    check(lib().bread_scale_accum_c(_p(dst), _p(src), scale, dst.numel(), _s(stream)), "bread_scale_accum")
+
+
+def copy_half(dst, src, stream=None) -> None:
+    check(lib().bread_copy_half_c(_p(dst), _p(src), dst.numel(), _s(stream)), "bread_copy_half")
+
+
+# ---- MoE block -------------------------------------------------------------
+def workspace_bytes(T: int, H: int, I: int, E: int, top_k: int) -> int:
+    return int(lib().bread_moe_workspace_bytes(T, H, I, E, top_k))
+
+
+def alloc_workspace(T: int, H: int, I: int, E: int, top_k: int, device="cuda"):
+    n = workspace_bytes(T, H, I, E, top_k)
+    return torch.empty(n + 256, dtype=torch.uint8, device=device)
+
+
+def _ws_ptr(ws):
+    base = ws.data_ptr()
+    return ctypes.c_void_p((base + 255) // 256 * 256), ws.numel() - ((base + 255) // 256 * 256 - base)
+
+
+def moe_route(x, W_r, w_sg, top_k: int, workspace=None, stream=None):
+    """route_layer (one_layer.cu:937-992) on the device for T tokens.
+    x [T, H] fp32, W_r [E, H] fp32, w_sg [H] fp16 or None.
+    Returns idx [T, k] int32, w [T, k] fp32, sg_weight [T] fp32."""
+    T, H = x.shape
+    E = W_r.shape[0]
+    if workspace is None:
+        workspace = alloc_workspace(T, H, 0, E, top_k, x.device)
+    wp, wn = _ws_ptr(workspace)
+    idx = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
+    w = torch.empty((T, top_k), dtype=torch.float32, device=x.device)
+    sg = torch.empty(T, dtype=torch.float32, device=x.device)
+    check(lib().bread_moe_route(_p(x), _p(W_r), _p(w_sg), T, H, E, top_k, _p(idx), _p(w), _p(sg), wp, wn,
+                                _s(stream)), "bread_moe_route")
+    return idx, w, sg
+
+
+def pointer_table(tensors_or_ptrs, device="cuda"):
+    """Device array of device pointers (the per-expert tables of loader.h:79-84)."""
+    ptrs = [t if isinstance(t, int) else t.data_ptr() for t in tensors_or_ptrs]
+    return torch.tensor(ptrs, dtype=torch.int64, device=device)
+
+
+def moe_ffn(gate_tab, up_tab, down_tab, W_r, w_sg, shared, x, out, I: int, top_k: int, workspace=None,
+            stream=None, want_routing: bool = False):
+    """One layer's MoE FFN for T tokens: out += sum_k w_k expert_k(x) + sg * shared(x).
+    *_tab: device int64 pointer tables [E]; shared: (gate, up, down) or None."""
+    T, H = x.shape
+    E = W_r.shape[0]
+    if workspace is None:
+        workspace = alloc_workspace(T, H, I, E, top_k, x.device)
+    wp, wn = _ws_ptr(workspace)
+    sh = (None, None, None) if shared is None else shared
+    idx = w = sg = None
+    if want_routing:
+        idx = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
+        w = torch.empty((T, top_k), dtype=torch.float32, device=x.device)
+        sg = torch.empty(T, dtype=torch.float32, device=x.device)
+    check(lib().bread_moe_ffn(_p(gate_tab), _p(up_tab), _p(down_tab), _p(W_r), _p(w_sg), _p(sh[0]), _p(sh[1]),
+                              _p(sh[2]), _p(x), _p(out), T, H, I, E, top_k, _p(idx), _p(w), _p(sg), wp, wn,
+                              _s(stream)), "bread_moe_ffn")
+    return (idx, w, sg) if want_routing else None
+
+
+# ---- expert stack ------------------------------------------------------------
+class ExpertStack:
+    """All layers' experts resident on this GPU (or this rank's share of them),
+    synthetic weights from a seed; ``step`` runs one decode step."""
+
+    def __init__(self, n_layers=40, hidden=2048, inter=512, n_experts=256, top_k=8, max_tokens=64,
+                 shared_expert=True, norm_eps=1e-6, seed=1234, rank=0, world=1):
+        self.cfg = StackConfig(n_layers, hidden, inter, n_experts, top_k, max_tokens, int(shared_expert), norm_eps,
+                               seed, rank, world)
+        h = ctypes.c_void_p(0)
+        check(lib().bread_stack_create(ctypes.byref(h), ctypes.byref(self.cfg)), "bread_stack_create")
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            lib().bread_stack_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def device_bytes(self) -> int:
+        return int(lib().bread_stack_device_bytes(self.handle))
+
+    def launches_per_step(self, T: int) -> int:
+        return int(lib().bread_stack_launches_per_step(self.handle, T))
+
+    def layer(self, l: int) -> dict:
+        ptrs = [ctypes.c_void_p(0) for _ in range(8)]
+        lo, hi = ctypes.c_int(0), ctypes.c_int(0)
+        check(lib().bread_stack_layer(self.handle, l, *[ctypes.byref(p) for p in ptrs], ctypes.byref(lo),
+                                      ctypes.byref(hi)), "bread_stack_layer")
+        keys = ["gate", "up", "down", "W_r", "w_sg", "sh_gate", "sh_up", "sh_down"]
+        d = {k: (p.value or 0) for k, p in zip(keys, ptrs)}
+        d["lo"], d["hi"] = lo.value, hi.value
+        return d
+
+    def step(self, h, stream=None) -> None:
+        """h: [T, hidden] fp32 on this device, updated in place."""
+        check(lib().bread_stack_step(self.handle, _p(h), h.shape[0], _s(stream)), "bread_stack_step")
+
+    def profile_step(self, h, stream=None):
+        """One instrumented step; returns per-layer (route, gate/up, down) ms."""
+        import numpy as np
+
+        L = self.cfg.n_layers
+        out = np.zeros(3 * L, dtype=np.float32)
+        check(lib().bread_stack_profile_step(self.handle, _p(h), h.shape[0], _s(stream),
+                                             out.ctypes.data_as(ctypes.c_void_p)), "bread_stack_profile_step")
+        return out.reshape(L, 3)
+
+    def routing_stats(self):
+        """Per layer of the last step: (expert groups computed here, token-expert pairs)."""
+        import numpy as np
+
+        L = self.cfg.n_layers
+        g = np.zeros(L, dtype=np.int32)
+        p = np.zeros(L, dtype=np.int32)
+        check(lib().bread_stack_routing_stats(self.handle, g.ctypes.data_as(ctypes.c_void_p),
+                                              p.ctypes.data_as(ctypes.c_void_p)), "bread_stack_routing_stats")
+        return g, p
+
+    def step_host(self, h_in, h_out, stream=None) -> None:
+        """h_in/h_out: [T, hidden] fp32 host tensors (pinned for speed)."""
+        check(lib().bread_stack_step_host(self.handle, _p(h_in), _p(h_out), h_in.shape[0], _s(stream)),
+              "bread_stack_step_host")
+
+
+# ---- synthetic data ----------------------------------------------------------
+def synth_blocks(n_blocks: int, qtype: int, seed: int, stream_id: int, device="cuda", stream=None):
+    out = torch.empty(n_blocks * BLOCK_BYTES[qtype], dtype=torch.uint8, device=device)
+    check(lib().bread_synth_blocks(_p(out), n_blocks, qtype, seed, stream_id, _s(stream)), "bread_synth_blocks")
+    return out
+
+
+def synth_blocks_host(n_blocks: int, qtype: int, seed: int, stream_id: int):
+    import numpy as np
+    out = np.empty(n_blocks * BLOCK_BYTES[qtype], dtype=np.uint8)
+    check(lib().bread_synth_blocks_host(out.ctypes.data_as(ctypes.c_void_p), n_blocks, qtype, seed, stream_id),
+          "bread_synth_blocks_host")
+    return out
+
+
+def synth_normal_host(n: int, stddev: float, seed: int, stream_id: int, half: bool = False):
+    import numpy as np
+    out = np.empty(n, dtype=np.uint16 if half else np.float32)
+    fn = lib().bread_synth_normal_f16_host if half else lib().bread_synth_normal_f32_host
+    check(fn(out.ctypes.data_as(ctypes.c_void_p), n, stddev, seed, stream_id), "bread_synth_normal_host")
+    return out
+
+
+def synth_normal(n: int, stddev: float, seed: int, stream_id: int, half: bool = False, device="cuda", stream=None):
+    out = torch.empty(n, dtype=torch.float16 if half else torch.float32, device=device)
+    fn = lib().bread_synth_normal_f16 if half else lib().bread_synth_normal_f32
+    check(fn(_p(out), n, stddev, seed, stream_id, _s(stream)), "bread_synth_normal")
+    return out

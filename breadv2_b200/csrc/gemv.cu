@@ -1,0 +1,412 @@
+// gemv.cu -- Q4_K / Q6_K / Q8_0 dequantise-and-multiply GEMV for sm_100a and
+// the bread_matvec family of entry points (reference kernels.cu:150-308).
+//
+// Fast path (Q4_K / Q6_K, 16-byte aligned weights, cols/256 in {1,2,4,8,16}):
+//   * every warp owns a contiguous range of rows and streams them through its
+//     own ring of shared-memory stages with 1-D bulk copies (TMA engine,
+//     completion on an mbarrier), so no registers are tied up by loads in
+//     flight and each weight byte crosses HBM once;
+//   * 4 lanes share a super-block (each lane decodes 64 weights), so a warp
+//     covers 32/(4*cols/256) rows per step;
+//   * the activation is quantised once per CTA to int16 per 32 values and
+//     each lane keeps its 64-value slice in registers (one token) or reloads
+//     it from shared memory per token (several tokens);
+//   * weight x activation products are exact int32 dp2a sums per sub-block,
+//     scaled in fp32 (qdot.cuh).
+// Generic path (any alignment, any cols multiple of the block, Q8_0): one warp
+// per row, exact fp32 dequantisation per element, fp32 FMA.
+#include <stdio.h>
+#include <stdlib.h>
+
+#include "common.cuh"
+#include "ptx.cuh"
+#include "qdot.cuh"
+
+namespace bread {
+
+template <int QT, int NB>
+struct Geo {
+    static constexpr int BB = QT == BREAD_QTYPE_Q4_K ? Q4K_BYTES : Q6K_BYTES;
+    static constexpr int LANES_ALL = 4 * NB;  // 4 lanes per super-block
+    static constexpr int CP = LANES_ALL > 32 ? LANES_ALL / 32 : 1;  // column passes per lane
+    static constexpr int LPR = LANES_ALL > 32 ? 32 : LANES_ALL;      // lanes per row
+    static constexpr int RPW = 32 / LPR;                              // rows per warp step
+    static constexpr int ROWB = BB * NB;
+    static constexpr int STEPB = ROWB * RPW;  // a multiple of 16 for every NB above
+    static constexpr int COLS = QK * NB;
+};
+
+constexpr int GEMV_WARPS = 8;
+constexpr int GEMV_STAGES = 3;   // shared-memory stages per warp
+constexpr int GEMV_TMAX = 8;     // tokens per launch on the fast path
+
+// warp steps per bulk copy: copies of about 2.3 - 3.5 KB
+template <int STEPB>
+struct Chunk {
+    static constexpr int CH = STEPB >= 3000 ? 1 : (STEPB >= 1500 ? 2 : 3);
+};
+
+__host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+template <int QT, int NB>
+struct GemvSmem {
+    static constexpr int CH = Chunk<Geo<QT, NB>::STEPB>::CH;
+    static constexpr size_t chunk = (size_t)Geo<QT, NB>::STEPB * CH;
+    static size_t bytes(int T)
+    {
+        size_t b = align_up((size_t)T * Geo<QT, NB>::COLS * 2, 16);           // xq
+        b += align_up((size_t)T * Geo<QT, NB>::COLS / 32 * 4, 16);             // xs
+        b += (size_t)GEMV_WARPS * GEMV_STAGES * chunk + 16;                    // stages + tail pad
+        b = align_up(b, 8) + GEMV_WARPS * GEMV_STAGES * 8;                     // mbarriers
+        return b;
+    }
+};
+
+// Quantise T x cols activations (fp32 or fp16) into shared memory.
+template <bool IN_HALF>
+__device__ __forceinline__ void quantise_to_smem(const void *x, int T, int cols, int16_t *xq, float *xs, int warp,
+                                                 int nwarps, int lane)
+{
+    const int groups = T * cols / 32;
+    for (int gi = warp; gi < groups; gi += nwarps) {
+        const int idx = gi * 32 + lane;
+        const float v = IN_HALF ? __half2float(reinterpret_cast<const __half *>(x)[idx])
+                                : reinterpret_cast<const float *>(x)[idx];
+        const int q = quant32(v, xs + gi, lane);
+        xq[idx] = (int16_t)q;
+    }
+}
+
+template <int QT, int NB, bool ONE_TOKEN, bool IN_HALF, bool OUT_HALF>
+__global__ void __launch_bounds__(GEMV_WARPS * 32)
+gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__restrict__ x, int T,
+                void *__restrict__ y, int rows_total)
+{
+    using G = Geo<QT, NB>;
+    constexpr size_t CHUNK = GemvSmem<QT, NB>::chunk;
+    constexpr int GEMV_CH = GemvSmem<QT, NB>::CH;
+    extern __shared__ __align__(128) uint8_t smem[];
+    int16_t *xq = reinterpret_cast<int16_t *>(smem);
+    float *xs = reinterpret_cast<float *>(smem + align_up((size_t)T * G::COLS * 2, 16));
+    uint8_t *stages = smem + align_up((size_t)T * G::COLS * 2, 16) + align_up((size_t)T * G::COLS / 32 * 4, 16);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(
+        smem + align_up(align_up((size_t)T * G::COLS * 2, 16) + align_up((size_t)T * G::COLS / 32 * 4, 16) +
+                            (size_t)GEMV_WARPS * GEMV_STAGES * CHUNK + 16,
+                        8));
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint8_t *my_stage = stages + (size_t)warp * GEMV_STAGES * CHUNK;
+    uint64_t *my_bar = bars + warp * GEMV_STAGES;
+
+    // this warp's step range
+    const long long wtot = (long long)gridDim.x * GEMV_WARPS;
+    const long long wid = (long long)blockIdx.x * GEMV_WARPS + warp;
+    const long long s0 = wid * nsteps / wtot, s1 = (wid + 1) * nsteps / wtot;
+    const int nst = (int)(s1 - s0);
+    const int nchunks = (nst + GEMV_CH - 1) / GEMV_CH;
+
+    if (lane == 0) {
+        for (int s = 0; s < GEMV_STAGES; ++s) mbar_init(my_bar + s, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    auto issue = [&](int c) {
+        const int first = c * GEMV_CH;
+        const int n = min(GEMV_CH, nst - first);
+        const unsigned bytes = (unsigned)(n * G::STEPB);
+        uint64_t *bar = my_bar + (c % GEMV_STAGES);
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(my_stage + (size_t)(c % GEMV_STAGES) * CHUNK, W + (s0 + first) * (long long)G::STEPB, bytes, bar);
+    };
+    if (lane == 0)
+        for (int c = 0; c < min(GEMV_STAGES, nchunks); ++c) issue(c);
+
+    quantise_to_smem<IN_HALF>(x, T, G::COLS, xq, xs, warp, GEMV_WARPS, lane);
+    __syncthreads();
+
+    // lane geometry
+    const int rho = lane / G::LPR;        // row within the warp step
+    const int lr = lane % G::LPR;         // lane within the row
+    const int bb = lr >> 2;               // block within the pass
+    const int sub = lr & 3;               // Q4_K: pair g; Q6_K: (h, g) = (sub >> 1, sub & 1)
+    Q6Lane L6;
+    if (QT == BREAD_QTYPE_Q6_K) {
+        // byte offset of this lane's block inside a 16-aligned step: 210*k, k = rho*NB + bb (+8 per pass)
+        L6 = q6_lane(((rho * NB + bb) & 1) ? 2 : 0, sub & 1);
+    }
+    auto slice_of = [&](XSlice &X, int t, int cp) {
+        const int b = cp * 8 + bb;
+        if (QT == BREAD_QTYPE_Q4_K)
+            load_slice_q4k(X, xq + (size_t)t * G::COLS, xs + (size_t)t * G::COLS / 32, QK * b + 64 * sub);
+        else
+            load_slice_q6k(X, xq + (size_t)t * G::COLS, xs + (size_t)t * G::COLS / 32, QK * b + 128 * (sub >> 1),
+                           sub & 1);
+    };
+    XSlice X1[ONE_TOKEN ? G::CP : 1];
+    if (ONE_TOKEN) {
+#pragma unroll
+        for (int cp = 0; cp < G::CP; ++cp) slice_of(X1[cp], 0, cp);
+    }
+
+    for (int c = 0; c < nchunks; ++c) {
+        const int slot = c % GEMV_STAGES;
+        if (!mbar_wait(my_bar + slot, (unsigned)((c / GEMV_STAGES) & 1))) return;
+        const uint8_t *buf = my_stage + (size_t)slot * CHUNK;
+        const int n = min(GEMV_CH, nst - c * GEMV_CH);
+        for (int st = 0; st < n; ++st) {
+            const long long row = (s0 + c * GEMV_CH + st) * G::RPW + rho;
+            const uint8_t *rowp = buf + (size_t)st * G::STEPB + (size_t)rho * G::ROWB;
+            float acc[ONE_TOKEN ? 1 : GEMV_TMAX];
+#pragma unroll
+            for (int t = 0; t < (ONE_TOKEN ? 1 : GEMV_TMAX); ++t) acc[t] = 0.0f;
+#pragma unroll
+            for (int cp = 0; cp < G::CP; ++cp) {
+                const uint8_t *blk = rowp + (size_t)(cp * 8 + bb) * G::BB;
+                if (ONE_TOKEN) {
+                    acc[0] += QT == BREAD_QTYPE_Q4_K ? q4k_lane_dot(blk, sub, X1[cp])
+                                                     : q6k_lane_dot(blk, sub >> 1, sub & 1, L6, X1[cp]);
+                } else {
+#pragma unroll
+                    for (int t = 0; t < GEMV_TMAX; ++t) {
+                        if (t < T) {
+                            XSlice X;
+                            slice_of(X, t, cp);
+                            acc[t] += QT == BREAD_QTYPE_Q4_K ? q4k_lane_dot(blk, sub, X)
+                                                             : q6k_lane_dot(blk, sub >> 1, sub & 1, L6, X);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < (ONE_TOKEN ? 1 : GEMV_TMAX); ++t) {
+                if (ONE_TOKEN || t < T) {
+                    float v = acc[t];
+#pragma unroll
+                    for (int o = G::LPR / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (lr == 0) {
+                        const size_t oi = (size_t)t * rows_total + row;
+                        if (OUT_HALF)
+                            reinterpret_cast<__half *>(y)[oi] = __float2half_rn(v);
+                        else
+                            reinterpret_cast<float *>(y)[oi] = v;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && c + GEMV_STAGES < nchunks) {
+            fence_proxy_async_smem();
+            issue(c + GEMV_STAGES);
+        }
+    }
+}
+
+// One warp per row; exact element dequantisation; any alignment.
+template <int QT, bool IN_HALF, bool OUT_HALF>
+__global__ void gemv_generic_kernel(const uint8_t *__restrict__ W, int row0, int rows, int cols, const void *x, int T,
+                                    void *y, int rows_total)
+{
+    constexpr int BE = QT == BREAD_QTYPE_Q8_0 ? Q80_ELEMS : QK;
+    constexpr int BBY = QT == BREAD_QTYPE_Q4_K ? Q4K_BYTES : QT == BREAD_QTYPE_Q6_K ? Q6K_BYTES : Q80_BYTES;
+    const int lane = threadIdx.x & 31;
+    const int wpb = blockDim.x >> 5;
+    const int nb = cols / BE;
+    for (int r = blockIdx.x * wpb + (threadIdx.x >> 5); r < rows; r += gridDim.x * wpb) {
+        const int row = row0 + r;
+        const uint8_t *rp = W + (size_t)row * nb * BBY;
+        for (int t = 0; t < T; ++t) {
+            float acc = 0.0f;
+            for (int e = lane; e < cols; e += 32) {
+                const float w = elem_exact<QT>(rp + (size_t)(e / BE) * BBY, e % BE);
+                const size_t xi = (size_t)t * cols + e;
+                const float xv = IN_HALF ? __half2float(reinterpret_cast<const __half *>(x)[xi])
+                                         : reinterpret_cast<const float *>(x)[xi];
+                acc = fmaf(w, xv, acc);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0) {
+                const size_t oi = (size_t)t * rows_total + row;
+                if (OUT_HALF)
+                    reinterpret_cast<__half *>(y)[oi] = __float2half_rn(acc);
+                else
+                    reinterpret_cast<float *>(y)[oi] = acc;
+            }
+        }
+    }
+}
+
+// Bit-exact block dequantisation: one warp per block.
+template <int QT>
+__global__ void dequant_kernel(const uint8_t *__restrict__ W, float *__restrict__ out, long long n_blocks)
+{
+    constexpr int BE = QT == BREAD_QTYPE_Q8_0 ? Q80_ELEMS : QK;
+    constexpr int BBY = QT == BREAD_QTYPE_Q4_K ? Q4K_BYTES : QT == BREAD_QTYPE_Q6_K ? Q6K_BYTES : Q80_BYTES;
+    const int lane = threadIdx.x & 31;
+    const long long wpb = blockDim.x >> 5;
+    for (long long b = blockIdx.x * wpb + (threadIdx.x >> 5); b < n_blocks; b += (long long)gridDim.x * wpb) {
+        const uint8_t *blk = W + b * BBY;
+        for (int e = lane; e < BE; e += 32) out[b * BE + e] = elem_exact<QT>(blk, e);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host dispatch
+// ---------------------------------------------------------------------------
+template <int QT, int NB, bool ONE, bool IH, bool OH>
+static int launch_fast(const uint8_t *W, long long nsteps, const void *x, int T, void *y, int rows_total,
+                       cudaStream_t stream)
+{
+    auto kern = gemv_tma_kernel<QT, NB, ONE, IH, OH>;
+    const size_t smem = GemvSmem<QT, NB>::bytes(T);
+    static int per_sm = 0;  // per instantiation; the attribute covers the largest T
+    if (!per_sm) {
+        BREAD_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)GemvSmem<QT, NB>::bytes(ONE ? 1 : GEMV_TMAX)),
+                   "gemv: set smem attribute");
+        int n = 1;
+        BREAD_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, GEMV_WARPS * 32,
+                                                                 GemvSmem<QT, NB>::bytes(ONE ? 1 : GEMV_TMAX)),
+                   "gemv occupancy");
+        per_sm = n < 1 ? 1 : n;
+    }
+    const long long want = (nsteps + GEMV_WARPS - 1) / GEMV_WARPS;
+    const long long cap = (long long)sm_count() * per_sm;
+    const int grid = (int)(want < cap ? want : cap);
+    kern<<<grid, GEMV_WARPS * 32, smem, stream>>>(W, nsteps, x, T, y, rows_total);
+    BREAD_CUDA(cudaGetLastError(), "gemv fast launch");
+    return BREAD_OK;
+}
+
+template <int QT, bool IH, bool OH>
+static int launch_generic(const uint8_t *W, int row0, int rows, int cols, const void *x, int T, void *y,
+                          int rows_total, cudaStream_t stream)
+{
+    if (rows <= 0) return BREAD_OK;
+    const int warps = 8;
+    long long want = ((long long)rows + warps - 1) / warps;
+    const long long cap = (long long)sm_count() * 8;
+    const int grid = (int)(want < cap ? want : cap);
+    gemv_generic_kernel<QT, IH, OH><<<grid, warps * 32, 0, stream>>>(W, row0, rows, cols, x, T, y, rows_total);
+    BREAD_CUDA(cudaGetLastError(), "gemv generic launch");
+    return BREAD_OK;
+}
+
+template <int QT, bool IH, bool OH>
+static int gemv_dispatch_q(const uint8_t *W, int rows, int cols, const void *x, int T, void *y, cudaStream_t stream)
+{
+    const int nb = cols / QK;
+    const bool aligned = (reinterpret_cast<uintptr_t>(W) & 15) == 0;
+    int rpw = 0;
+    if (aligned && (nb == 1 || nb == 2 || nb == 4 || nb == 8 || nb == 16)) rpw = nb >= 8 ? 1 : 8 / nb;
+    if (!rpw) return launch_generic<QT, IH, OH>(W, 0, rows, cols, x, T, y, rows, stream);
+    const long long nsteps = rows / rpw;
+    const int rows_main = (int)(nsteps * rpw);
+    if (nsteps > 0) {
+        int st = BREAD_OK;
+        const bool one = T == 1;
+#define BREAD_FAST(NB_)                                                                                \
+    case NB_:                                                                                          \
+        st = one ? launch_fast<QT, NB_, true, IH, OH>(W, nsteps, x, T, y, rows, stream)                \
+                 : launch_fast<QT, NB_, false, IH, OH>(W, nsteps, x, T, y, rows, stream);             \
+        break;
+        switch (nb) {
+            BREAD_FAST(1)
+            BREAD_FAST(2)
+            BREAD_FAST(4)
+            BREAD_FAST(8)
+            BREAD_FAST(16)
+        default: break;
+        }
+#undef BREAD_FAST
+        if (st != BREAD_OK) return st;
+    }
+    return launch_generic<QT, IH, OH>(W, rows_main, rows - rows_main, cols, x, T, y, rows, stream);
+}
+
+// y[T x rows] = x[T x cols] * W^T for T <= GEMV_TMAX.
+template <bool IH, bool OH>
+static int gemv_any(const void *w, int qtype, int rows, int cols, const void *x, int T, void *y, cudaStream_t stream)
+{
+    const uint8_t *W = static_cast<const uint8_t *>(w);
+    switch (qtype) {
+    case BREAD_QTYPE_Q4_K: return gemv_dispatch_q<BREAD_QTYPE_Q4_K, IH, OH>(W, rows, cols, x, T, y, stream);
+    case BREAD_QTYPE_Q6_K: return gemv_dispatch_q<BREAD_QTYPE_Q6_K, IH, OH>(W, rows, cols, x, T, y, stream);
+    case BREAD_QTYPE_Q8_0: return launch_generic<BREAD_QTYPE_Q8_0, IH, OH>(W, 0, rows, cols, x, T, y, rows, stream);
+    default: return set_error(BREAD_ERR_QTYPE, "unknown qtype %d", qtype);
+    }
+}
+
+static int check_gemv_args(const void *w, const void *x, const void *y, int rows, int cols, int qtype, int T)
+{
+    if (!w || !x || !y) return set_error(BREAD_ERR_ARG, "matvec: NULL pointer");
+    const int be = block_elems(qtype);
+    if (!block_bytes(qtype)) return set_error(BREAD_ERR_QTYPE, "matvec: unknown qtype %d", qtype);
+    if (rows <= 0 || cols <= 0 || cols % be) return set_error(BREAD_ERR_ARG, "matvec: rows=%d cols=%d (cols must be a positive multiple of %d)", rows, cols, be);
+    if (T < 1 || T > 64) return set_error(BREAD_ERR_ARG, "matvec: T=%d outside 1..64", T);
+    if (reinterpret_cast<uintptr_t>(x) & 3) return set_error(BREAD_ERR_ALIGN, "matvec: x not 4-byte aligned");
+    return BREAD_OK;
+}
+
+}  // namespace bread
+
+using namespace bread;
+
+extern "C" int bread_matvec_f32(const void *w, const float *x, float *y, int rows, int cols, int qtype,
+                                cudaStream_t stream)
+{
+    BREAD_TRY(check_gemv_args(w, x, y, rows, cols, qtype, 1));
+    return gemv_any<false, false>(w, qtype, rows, cols, x, 1, y, stream);
+}
+
+extern "C" int bread_matvec_f16(const void *w, const void *x, void *y, int rows, int cols, int qtype,
+                                cudaStream_t stream)
+{
+    if (!w || !x || !y) return set_error(BREAD_ERR_ARG, "matvec: NULL pointer");
+    if (!block_bytes(qtype)) return set_error(BREAD_ERR_QTYPE, "unknown qtype %d", qtype);
+    if (rows <= 0 || cols <= 0 || cols % block_elems(qtype)) return set_error(BREAD_ERR_ARG, "matvec: rows=%d cols=%d", rows, cols);
+    if (reinterpret_cast<uintptr_t>(x) & 1) return set_error(BREAD_ERR_ALIGN, "matvec: x not 2-byte aligned");
+    return gemv_any<true, true>(w, qtype, rows, cols, x, 1, y, stream);
+}
+
+extern "C" int bread_matvec_batch_f32(const void *w, const float *x, float *y, int rows, int cols, int qtype, int T,
+                                      cudaStream_t stream)
+{
+    BREAD_TRY(check_gemv_args(w, x, y, rows, cols, qtype, T));
+    // token chunks of GEMV_TMAX: each chunk streams the weights once
+    for (int t0 = 0; t0 < T; t0 += GEMV_TMAX) {
+        const int n = T - t0 < GEMV_TMAX ? T - t0 : GEMV_TMAX;
+        BREAD_TRY(gemv_any<false, false>(w, qtype, rows, cols, x + (size_t)t0 * cols, n, y + (size_t)t0 * rows,
+                                         stream));
+    }
+    return BREAD_OK;
+}
+
+extern "C" int bread_dequant(const void *w, float *out, long long n_blocks, int qtype, cudaStream_t stream)
+{
+    if (!w || !out || n_blocks < 0) return set_error(BREAD_ERR_ARG, "dequant: bad argument");
+    if (n_blocks == 0) return BREAD_OK;
+    const long long want = (n_blocks + 7) / 8;
+    const long long cap = (long long)sm_count() * 16;
+    const int grid = (int)(want < cap ? want : cap);
+    const uint8_t *W = static_cast<const uint8_t *>(w);
+    switch (qtype) {
+    case BREAD_QTYPE_Q4_K: dequant_kernel<BREAD_QTYPE_Q4_K><<<grid, 256, 0, stream>>>(W, out, n_blocks); break;
+    case BREAD_QTYPE_Q6_K: dequant_kernel<BREAD_QTYPE_Q6_K><<<grid, 256, 0, stream>>>(W, out, n_blocks); break;
+    case BREAD_QTYPE_Q8_0: dequant_kernel<BREAD_QTYPE_Q8_0><<<grid, 256, 0, stream>>>(W, out, n_blocks); break;
+    default: return set_error(BREAD_ERR_QTYPE, "dequant: unknown qtype %d", qtype);
+    }
+    BREAD_CUDA(cudaGetLastError(), "dequant launch");
+    return BREAD_OK;
+}
+
+// Drop-in for kernels.cu:289 (C++ linkage, same signature): aborts on error
+// like the reference's CUDA_CHECK / unknown-qtype exit.
+void bread_matvec(void *w, half *x, half *y, int rows, int cols, int qtype, cudaStream_t stream)
+{
+    const int st = bread_matvec_f16(w, x, y, rows, cols, qtype, stream);
+    if (st != BREAD_OK) {
+        fprintf(stderr, "bread_matvec: %s (%s)\n", bread_status_string(st), bread_last_error());
+        exit(1);
+    }
+}

@@ -1,0 +1,750 @@
+// moe.cu -- the MoE FFN block on sm_100a: device router with top-k (K1), one
+// grouped gate/up + SiLU*mul launch over every active expert (K2), one grouped
+// down launch fused with the router-weighted combine (K3).
+//
+// Reference path replaced: route_layer (one_layer.cu:937-992, with
+// cpu_softmax/cpu_topk layer_ops.cu:222-250), the shared expert
+// (one_layer.cu:1840-1894) and the serial expert loop (one_layer.cu:1931-1983:
+// per expert bread_matvec gate, up, silu_mul_inplace, bread_matvec down,
+// scale_accum).
+//
+// Data flow for T tokens (all in the caller's workspace):
+//   K1  every CTA: quantise a slice of x to int16 (+ per-group sum of squares)
+//       and compute two router rows (fp32 GEMV, fixed-order reduction);
+//       the last CTA to finish (atomic ticket) does the softmax + top-k per
+//       token and groups the (token, slot) pairs by expert: group 0 is the
+//       shared expert (every token), then the routed experts in ascending id.
+//   K2  persistent CTAs walk work items (group, token chunk of <= 8, 32 rows):
+//       a producer warp streams the 32 gate rows and 32 up rows of the item
+//       into a shared-memory ring with bulk copies; 8 consumer warps dot them
+//       with each token's int16 activations, apply silu(g)*u and quantise the
+//       32 results (one activation group) to int16 for K3.
+//   K3  CTAs own 16 output rows each: the producer streams those 16 rows of
+//       every active expert's down matrix; consumers dot them with each pair's
+//       intermediate and accumulate w * result per (token, row) in per-warp
+//       shared-memory accumulators, summed in fixed warp order at the end, so
+//       the combine is deterministic and needs no atomics.
+#include <math.h>
+
+#include "common.cuh"
+#include "moe.cuh"
+#include "ptx.cuh"
+#include "qdot.cuh"
+
+namespace bread {
+
+template <int QT, int NB>
+struct MGeo {
+    static constexpr int BB = QT == BREAD_QTYPE_Q4_K ? Q4K_BYTES : Q6K_BYTES;
+    static constexpr int LANES_ALL = 4 * NB;
+    static constexpr int CP = LANES_ALL > 32 ? LANES_ALL / 32 : 1;
+    static constexpr int LPR = LANES_ALL > 32 ? 32 : LANES_ALL;
+    static constexpr int RPW = 32 / LPR;
+    static constexpr int ROWB = BB * NB;
+    static constexpr int STEPB = ROWB * RPW;
+};
+
+constexpr int K1_ROWS = 2;  // router rows per CTA (4 warps per row)
+
+// ---------------------------------------------------------------------------
+// K1: router + finalize
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ void moe_finalize(const MoeArgs &a)
+{
+    __shared__ int s_cnt[MOE_EMAX], s_run[MOE_EMAX], s_off[MOE_EMAX], s_gcnt[MOE_EMAX + 1];
+    __shared__ float s_rinv[MOE_TMAX];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int T = a.T, H = a.H, E = a.E, K = a.top_k, HG = H / 32;
+
+    // (a) RMS factors from the per-group sums of squares K1 wrote
+    for (int t = warp; t < T; t += 8) {
+        float ss = 0.0f;
+        for (int g = lane; g < HG; g += 32) ss += __ldcg(a.ssq + t * HG + g);
+        ss = warp_sum(ss);
+        if (lane == 0) s_rinv[t] = a.norm_eps >= 0.0f ? rsqrtf(ss / (float)H + a.norm_eps) : 1.0f;
+    }
+    for (int i = tid; i < MOE_EMAX; i += blockDim.x) {
+        s_cnt[i] = 0;
+        s_run[i] = 0;
+    }
+    __syncthreads();
+    // (b) activation scales of the normalised input
+    if (a.norm_eps >= 0.0f)
+        for (int i = tid; i < T * HG; i += blockDim.x) a.xs[i] = __ldcg(a.xs + i) * s_rinv[i / HG];
+
+    // (c) softmax + top-k, one warp per token (layer_ops.cu:222-250)
+    constexpr int PER = MOE_EMAX / 32;
+    for (int t = warp; t < T; t += 8) {
+        const float r = s_rinv[t];
+        float p[PER];
+        float m = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int e = lane + 32 * j;
+            p[j] = e < E ? __ldcg(a.logits + (size_t)t * E + e) * r : -INFINITY;
+            m = fmaxf(m, p[j]);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int e = lane + 32 * j;
+            p[j] = e < E ? expf(p[j] - m) : 0.0f;
+            s += p[j];
+        }
+        s = warp_sum(s);
+#pragma unroll
+        for (int j = 0; j < PER; ++j) p[j] = (lane + 32 * j) < E ? p[j] / s : -1.0f;
+        unsigned used = 0;
+        float wsum = 0.0f, my_w = 0.0f;
+        int my_i = 0;
+        for (int k = 0; k < K; ++k) {
+            float bv = -1e30f;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int j = 0; j < PER; ++j)
+                if (!((used >> j) & 1u) && p[j] > bv) {
+                    bv = p[j];
+                    bi = lane + 32 * j;
+                }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if ((bi & 31) == lane) used |= 1u << (bi >> 5);
+            if (lane == k) {
+                my_w = bv;
+                my_i = bi;
+            }
+            wsum += bv;
+        }
+        if (lane < K) {
+            const float w = wsum > 0.0f ? my_w / wsum : my_w;
+            a.ridx[t * K + lane] = my_i;
+            a.rw[t * K + lane] = w;
+            if (a.idx_out) a.idx_out[t * K + lane] = my_i;
+            if (a.w_out) a.w_out[t * K + lane] = w;
+        }
+        if (lane == 0) {
+            const float sg = a.w_sg ? 1.0f / (1.0f + expf(-(__ldcg(a.score + t) * r))) : 0.5f;
+            a.sgw[t] = sg;
+            if (a.sg_out) a.sg_out[t] = sg;
+        }
+    }
+    __syncthreads();
+
+    // (d) pairs per local expert
+    const int P = T * K;
+    for (int q = tid; q < P; q += blockDim.x) {
+        const int e = __ldcg(a.ridx + q);
+        if (e >= a.lo && e < a.hi) atomicAdd(&s_cnt[e - a.lo], 1);
+    }
+    __syncthreads();
+    if (warp != 0) return;
+
+    // (e) groups: shared expert first, then routed experts by ascending id
+    const int NL = a.hi - a.lo;
+    const int hs = a.shared_here ? 1 : 0;
+    int gbase = hs, pbase = hs ? T : 0;
+    if (hs && lane == 0) {
+        a.g_expert[0] = E;
+        a.g_off[0] = 0;
+        a.g_cnt[0] = T;
+        s_gcnt[0] = T;
+    }
+    for (int c0 = 0; c0 < NL; c0 += 32) {
+        const int el = c0 + lane;
+        const int cnt = el < NL ? s_cnt[el] : 0;
+        const int flag = cnt > 0 ? 1 : 0;
+        int fi = flag, ci = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int f = __shfl_up_sync(0xffffffffu, fi, o);
+            const int c = __shfl_up_sync(0xffffffffu, ci, o);
+            if (lane >= o) {
+                fi += f;
+                ci += c;
+            }
+        }
+        const int gid = gbase + fi - flag, off = pbase + ci - cnt;
+        if (flag) {
+            a.g_expert[gid] = a.lo + el;
+            a.g_off[gid] = off;
+            a.g_cnt[gid] = cnt;
+            s_gcnt[gid] = cnt;
+        }
+        if (el < NL) s_off[el] = off;
+        gbase += __shfl_sync(0xffffffffu, fi, 31);
+        pbase += __shfl_sync(0xffffffffu, ci, 31);
+    }
+    __syncwarp();
+    const int ng = gbase;
+    int cbase = 0;
+    for (int g0 = 0; g0 < ng; g0 += 32) {
+        const int g = g0 + lane;
+        const int ch = g < ng ? (s_gcnt[g] + MOE_TC - 1) / MOE_TC : 0;
+        int ci = ch;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int c = __shfl_up_sync(0xffffffffu, ci, o);
+            if (lane >= o) ci += c;
+        }
+        if (g < ng) a.g_cpre[g] = cbase + ci - ch;
+        cbase += __shfl_sync(0xffffffffu, ci, 31);
+    }
+    if (lane == 0) {
+        a.g_cpre[ng] = cbase;
+        a.g_off[ng] = pbase;
+        a.hdr[HDR_NGROUPS] = ng;
+        a.hdr[HDR_NCHUNKS] = cbase;
+        if (a.stats) {
+            a.stats[0] = ng;
+            a.stats[1] = pbase;
+        }
+    }
+    // (f) place pairs, token-major inside each expert (deterministic)
+    for (int q0 = 0; q0 < P; q0 += 32) {
+        const int q = q0 + lane;
+        int e = -1;
+        bool loc = false;
+        if (q < P) {
+            e = __ldcg(a.ridx + q);
+            loc = e >= a.lo && e < a.hi;
+        }
+        const unsigned act = __ballot_sync(0xffffffffu, loc);
+        if (loc) {
+            const unsigned peers = __match_any_sync(act, e);
+            const int rank = __popc(peers & ((1u << lane) - 1u));
+            const int el = e - a.lo;
+            const int pos = s_off[el] + s_run[el] + rank;
+            a.p_token[pos] = q / K;
+            a.p_w[pos] = __ldcg(a.rw + q);
+            if (__ffs(peers) - 1 == lane) s_run[el] += __popc(peers);
+        }
+        __syncwarp();
+    }
+    if (hs)
+        for (int t = lane; t < T; t += 32) {
+            a.p_token[t] = t;
+            a.p_w[t] = __ldcg(a.sgw + t);
+        }
+    if (lane == 0) a.hdr[HDR_TICKET] = 0;  // re-armed for the next launch
+}
+
+__global__ void __launch_bounds__(256) moe_route_kernel(MoeArgs a)
+{
+    __shared__ float s_part[K1_ROWS][4][MOE_TMAX];
+    __shared__ int s_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int T = a.T, H = a.H, E = a.E;
+    const int nrows = E + (a.w_sg ? 1 : 0);
+
+    // quantise x: T*H/32 groups over all warps of the grid
+    {
+        const int groups = T * (H / 32);
+        for (int gi = blockIdx.x * 8 + warp; gi < groups; gi += gridDim.x * 8) {
+            const float v = a.x[(size_t)gi * 32 + lane];
+            const float ss = warp_sum(v * v);
+            if (lane == 0) a.ssq[gi] = ss;
+            const int q = quant32(v, a.xs + gi, lane);
+            a.xq[(size_t)gi * 32 + lane] = (int16_t)q;
+        }
+    }
+    // router rows (row E is the fp16 shared-gate vector)
+    {
+        const int rl = warp >> 2, qt = warp & 3;
+        const int row = blockIdx.x * K1_ROWS + rl;
+        if (row < nrows) {
+            const int seg = H / 4;
+            const int c0 = qt * seg;
+            for (int t = 0; t < T; ++t) {
+                const float *xt = a.x + (size_t)t * H;
+                float acc = 0.0f;
+                if (row < E) {
+                    const float *wr = a.W_r + (size_t)row * H;
+                    for (int c = c0 + lane; c < c0 + seg; c += 32) acc = fmaf(wr[c], xt[c], acc);
+                } else {
+                    for (int c = c0 + lane; c < c0 + seg; c += 32) acc = fmaf(__half2float(a.w_sg[c]), xt[c], acc);
+                }
+                acc = warp_sum(acc);
+                if (lane == 0) s_part[rl][qt][t] = acc;
+            }
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < K1_ROWS * T; i += blockDim.x) {
+        const int rl = i / T, t = i % T;
+        const int row = blockIdx.x * K1_ROWS + rl;
+        if (row < nrows) {
+            const float v = ((s_part[rl][0][t] + s_part[rl][1][t]) + s_part[rl][2][t]) + s_part[rl][3][t];
+            if (row < E)
+                a.logits[(size_t)t * E + row] = v;
+            else
+                a.score[t] = v;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(reinterpret_cast<unsigned *>(a.hdr + HDR_TICKET), 1u);
+        s_last = prev == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    moe_finalize(a);
+}
+
+// ---------------------------------------------------------------------------
+// K2: gate/up + SiLU*mul
+// ---------------------------------------------------------------------------
+template <int NB>
+struct K2Cfg {
+    using G = MGeo<BREAD_QTYPE_Q4_K, NB>;
+    static constexpr int SR = 8 * G::RPW < MOE_ROWTILE ? 8 * G::RPW : MOE_ROWTILE;  // rows per stage
+    static constexpr int SPI = MOE_ROWTILE / SR;                                      // stages per item
+    static constexpr int STB = 2 * SR * G::ROWB;                                      // gate rows + up rows
+    static constexpr int NS = (150 * 1024) / STB;
+    static constexpr size_t BAR_OFF = (size_t)NS * STB + 16;
+    static constexpr size_t ABUF_OFF = BAR_OFF + 2 * NS * 8;
+    static constexpr size_t SMEM = ABUF_OFF + MOE_TC * MOE_ROWTILE * 4;
+};
+
+__device__ __forceinline__ void decode_item(const MoeArgs &a, int ng, int R, long long it, int &g, int &c, int &rt)
+{
+    const int cg = (int)(it / R);
+    rt = (int)(it % R);
+    int lo = 0, hi = ng - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.g_cpre[mid] <= cg)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    g = lo;
+    c = cg - a.g_cpre[g];
+}
+
+template <int NB>
+__global__ void __launch_bounds__(288) moe_gateup_kernel(MoeArgs a)
+{
+    using C = K2Cfg<NB>;
+    using G = typename C::G;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *stages = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *empty = full + C::NS;
+    float *abuf = reinterpret_cast<float *>(smem + C::ABUF_OFF);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        for (int s = 0; s < C::NS; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 8);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const int ng = a.hdr[HDR_NGROUPS];
+    const int R = a.I / MOE_ROWTILE;
+    const long long n_items = (long long)a.hdr[HDR_NCHUNKS] * R;
+
+    if (warp == 8) {  // producer
+        if (lane != 0) return;
+        int n = 0;
+        for (long long it = blockIdx.x; it < n_items; it += gridDim.x) {
+            int g, c, rt;
+            decode_item(a, ng, R, it, g, c, rt);
+            const int e = a.g_expert[g];
+            const uint8_t *gb = e >= a.E ? a.sh_gate : a.gate[e];
+            const uint8_t *ub = e >= a.E ? a.sh_up : a.up[e];
+            const bool ok = gb && ub && !((reinterpret_cast<uintptr_t>(gb) | reinterpret_cast<uintptr_t>(ub)) & 15);
+            if (!ok) flag_error(DEVERR_ROUTE);
+            for (int s = 0; s < C::SPI; ++s, ++n) {
+                const int slot = n % C::NS;
+                if (n >= C::NS && !mbar_wait(empty + slot, (unsigned)(((n / C::NS) - 1) & 1))) return;
+                const size_t r0 = (size_t)rt * MOE_ROWTILE + (size_t)s * C::SR;
+                const unsigned bytes = (unsigned)(C::SR * G::ROWB);
+                if (ok) {
+                    mbar_arrive_expect_tx(full + slot, 2 * bytes);
+                    bulk_g2s(stages + (size_t)slot * C::STB, gb + r0 * G::ROWB, bytes, full + slot);
+                    bulk_g2s(stages + (size_t)slot * C::STB + bytes, ub + r0 * G::ROWB, bytes, full + slot);
+                } else {
+                    mbar_arrive(full + slot);
+                }
+            }
+        }
+        return;
+    }
+
+    // consumers: warps 0..7
+    const int rho = lane / G::LPR, lr = lane % G::LPR, bb = lr >> 2, sub = lr & 3;
+    XSlice X[G::CP];
+    int cached = -1;
+    int n = 0;
+    for (long long it = blockIdx.x; it < n_items; it += gridDim.x) {
+        int g, c, rt;
+        decode_item(a, ng, R, it, g, c, rt);
+        const int p0 = a.g_off[g] + c * MOE_TC;
+        const int np = min(MOE_TC, a.g_cnt[g] - c * MOE_TC);
+        for (int s = 0; s < C::SPI; ++s, ++n) {
+            const int slot = n % C::NS;
+            if (!mbar_wait(full + slot, (unsigned)((n / C::NS) & 1))) return;
+            const int rs = warp * G::RPW + rho;  // row inside the stage
+            const uint8_t *grow = stages + (size_t)slot * C::STB + (size_t)rs * G::ROWB;
+            const uint8_t *urow = grow + (size_t)C::SR * G::ROWB;
+            // with 8 rows per warp step (H = 256) only warps 0..3 have rows
+            const int nj = warp * G::RPW < C::SR ? np : 0;
+            for (int j = 0; j < nj; ++j) {
+                const int t = a.p_token[p0 + j];
+                if (t != cached) {
+#pragma unroll
+                    for (int cp = 0; cp < G::CP; ++cp)
+                        load_slice_q4k(X[cp], a.xq + (size_t)t * a.H, a.xs + (size_t)t * (a.H / 32),
+                                       QK * (cp * 8 + bb) + 64 * sub);
+                    cached = t;
+                }
+                float gs = 0.0f, us = 0.0f;
+#pragma unroll
+                for (int cp = 0; cp < G::CP; ++cp) {
+                    gs += q4k_lane_dot(grow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                    us += q4k_lane_dot(urow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                }
+#pragma unroll
+                for (int o = G::LPR / 2; o; o >>= 1) {
+                    gs += __shfl_xor_sync(0xffffffffu, gs, o);
+                    us += __shfl_xor_sync(0xffffffffu, us, o);
+                }
+                if (lr == 0) abuf[j * MOE_ROWTILE + s * C::SR + rs] = gs / (1.0f + expf(-gs)) * us;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty + slot);
+        }
+        named_sync(1, 256);
+        for (int j = warp; j < np; j += 8) {
+            const size_t p = (size_t)(p0 + j);
+            const int q = quant32(abuf[j * MOE_ROWTILE + lane], a.as + p * (a.I / 32) + rt, lane);
+            a.aq[p * a.I + (size_t)rt * MOE_ROWTILE + lane] = (int16_t)q;
+        }
+        named_sync(1, 256);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// K3: down + weighted combine
+// ---------------------------------------------------------------------------
+template <int NB>
+struct K3Cfg {
+    using G = MGeo<BREAD_QTYPE_Q6_K, NB>;
+    static constexpr int WS = MOE_RT3 / G::RPW;  // warp steps per group stage
+    static constexpr int STB = MOE_RT3 * G::ROWB;
+    static constexpr int NS = (96 * 1024) / STB < 2 ? 2 : (96 * 1024) / STB;
+    static constexpr size_t BAR_OFF = (size_t)NS * STB + 16;
+    static constexpr size_t ACC_OFF = BAR_OFF + 2 * NS * 8;
+    static size_t smem(int T) { return ACC_OFF + (size_t)8 * T * MOE_RT3 * 4; }
+};
+
+template <int NB>
+__global__ void __launch_bounds__(288) moe_down_kernel(MoeArgs a)
+{
+    using C = K3Cfg<NB>;
+    using G = typename C::G;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *stages = smem;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *empty = full + C::NS;
+    float *accs = reinterpret_cast<float *>(smem + C::ACC_OFF);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int T = a.T;
+    if (tid == 0) {
+        for (int s = 0; s < C::NS; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, C::WS);
+        }
+        fence_mbar_init();
+    }
+    for (int i = tid; i < 8 * T * MOE_RT3; i += blockDim.x) accs[i] = 0.0f;
+    __syncthreads();
+    const int ng = a.hdr[HDR_NGROUPS];
+    const int n_items = a.H / MOE_RT3;
+
+    if (warp == 8) {  // producer
+        if (lane != 0) return;
+        int n = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+            for (int g = 0; g < ng; ++g, ++n) {
+                const int slot = n % C::NS;
+                if (n >= C::NS && !mbar_wait(empty + slot, (unsigned)(((n / C::NS) - 1) & 1))) return;
+                const int e = a.g_expert[g];
+                const uint8_t *db = e >= a.E ? a.sh_down : a.down[e];
+                const bool ok = db && !(reinterpret_cast<uintptr_t>(db) & 15);
+                if (ok) {
+                    mbar_arrive_expect_tx(full + slot, (unsigned)C::STB);
+                    bulk_g2s(stages + (size_t)slot * C::STB, db + (size_t)it * MOE_RT3 * G::ROWB, (unsigned)C::STB,
+                             full + slot);
+                } else {
+                    flag_error(DEVERR_ROUTE);
+                    mbar_arrive(full + slot);
+                }
+            }
+        }
+        return;
+    }
+
+    const int rho = lane / G::LPR, lr = lane % G::LPR, bb = lr >> 2, sub = lr & 3;
+    const Q6Lane L6 = q6_lane(((rho * NB + bb) & 1) ? 2 : 0, sub & 1);
+    float *my_acc = accs + (size_t)warp * T * MOE_RT3;
+    int n = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+        for (int g = 0; g < ng; ++g, ++n) {
+            const int slot = n % C::NS;
+            const int pbeg = a.g_off[g], pend = pbeg + a.g_cnt[g];
+            bool waited = false;
+            for (int ws = 0; ws < C::WS; ++ws) {
+                if (((g * C::WS + ws) & 7) != warp) continue;
+                if (!waited) {
+                    if (!mbar_wait(full + slot, (unsigned)((n / C::NS) & 1))) return;
+                    waited = true;
+                }
+                const uint8_t *rowp = stages + (size_t)slot * C::STB + (size_t)ws * G::STEPB + (size_t)rho * G::ROWB;
+                for (int p = pbeg; p < pend; ++p) {
+                    const int t = a.p_token[p];
+                    const float wgt = a.p_w[p];
+                    float v = 0.0f;
+#pragma unroll
+                    for (int cp = 0; cp < G::CP; ++cp) {
+                        XSlice X;
+                        load_slice_q6k(X, a.aq + (size_t)p * a.I, a.as + (size_t)p * (a.I / 32),
+                                       QK * (cp * 8 + bb) + 128 * (sub >> 1), sub & 1);
+                        v += q6k_lane_dot(rowp + (size_t)(cp * 8 + bb) * Q6K_BYTES, sub >> 1, sub & 1, L6, X);
+                    }
+#pragma unroll
+                    for (int o = G::LPR / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (lr == 0) my_acc[t * MOE_RT3 + ws * G::RPW + rho] += wgt * v;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty + slot);
+            }
+        }
+        named_sync(1, 256);
+        for (int i = tid; i < T * MOE_RT3; i += 256) {
+            const int t = i / MOE_RT3, r = i % MOE_RT3;
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+                s += accs[(size_t)w * T * MOE_RT3 + i];
+                accs[(size_t)w * T * MOE_RT3 + i] = 0.0f;
+            }
+            float *o = a.out + (size_t)t * a.H + (size_t)it * MOE_RT3 + r;
+            *o = *o + s;
+        }
+        named_sync(1, 256);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+void moe_bind_workspace(MoeArgs &a, void *ws, const MoeWs &L)
+{
+    uint8_t *b = static_cast<uint8_t *>(ws);
+    a.hdr = reinterpret_cast<int *>(b + L.hdr);
+    a.logits = reinterpret_cast<float *>(b + L.logits);
+    a.ssq = reinterpret_cast<float *>(b + L.ssq);
+    a.score = reinterpret_cast<float *>(b + L.score);
+    a.ridx = reinterpret_cast<int *>(b + L.ridx);
+    a.rw = reinterpret_cast<float *>(b + L.rw);
+    a.sgw = reinterpret_cast<float *>(b + L.sgw);
+    a.xq = reinterpret_cast<int16_t *>(b + L.xq);
+    a.xs = reinterpret_cast<float *>(b + L.xs);
+    a.g_expert = reinterpret_cast<int *>(b + L.g_expert);
+    a.g_off = reinterpret_cast<int *>(b + L.g_off);
+    a.g_cnt = reinterpret_cast<int *>(b + L.g_cnt);
+    a.g_cpre = reinterpret_cast<int *>(b + L.g_cpre);
+    a.p_token = reinterpret_cast<int *>(b + L.p_token);
+    a.p_w = reinterpret_cast<float *>(b + L.p_w);
+    a.aq = reinterpret_cast<int16_t *>(b + L.aq);
+    a.as = reinterpret_cast<float *>(b + L.as);
+}
+
+static bool nb_ok_h(int nb) { return nb == 1 || nb == 2 || nb == 4 || nb == 8 || nb == 16; }
+static bool nb_ok_i(int nb) { return nb == 1 || nb == 2 || nb == 4 || nb == 8; }
+
+int moe_check_shapes(int T, int H, int I, int E, int top_k, bool need_experts)
+{
+    if (T < 1 || T > MOE_TMAX) return set_error(BREAD_ERR_ARG, "moe: T=%d outside 1..%d", T, MOE_TMAX);
+    if (top_k < 1 || top_k > MOE_KMAX || E < top_k || E > MOE_EMAX)
+        return set_error(BREAD_ERR_ARG, "moe: E=%d top_k=%d (need 1 <= top_k <= %d, top_k <= E <= %d)", E, top_k,
+                         MOE_KMAX, MOE_EMAX);
+    if (H < 256 || H > MOE_HMAX || H % 256 || !nb_ok_h(H / 256))
+        return set_error(BREAD_ERR_ARG, "moe: H=%d (need H/256 in {1,2,4,8,16})", H);
+    if (need_experts && (I < 256 || I > MOE_IMAX || I % 256 || !nb_ok_i(I / 256)))
+        return set_error(BREAD_ERR_ARG, "moe: I=%d (need I/256 in {1,2,4,8})", I);
+    return BREAD_OK;
+}
+
+int moe_route_grid(const MoeArgs &a) { return (a.E + (a.w_sg ? 1 : 0) + K1_ROWS - 1) / K1_ROWS; }
+
+int moe_launch_route(const MoeArgs &a, cudaStream_t s)
+{
+    moe_route_kernel<<<moe_route_grid(a), 256, 0, s>>>(a);
+    BREAD_CUDA(cudaGetLastError(), "moe route launch");
+    return BREAD_OK;
+}
+
+template <int NB>
+static int launch_gateup_nb(const MoeArgs &a, cudaStream_t s)
+{
+    using C = K2Cfg<NB>;
+    static bool attr = false;
+    if (!attr) {
+        BREAD_CUDA(cudaFuncSetAttribute(moe_gateup_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM),
+                   "moe gate/up smem attribute");
+        attr = true;
+    }
+    moe_gateup_kernel<NB><<<sm_count(), 288, C::SMEM, s>>>(a);
+    BREAD_CUDA(cudaGetLastError(), "moe gate/up launch");
+    return BREAD_OK;
+}
+
+int moe_launch_gateup(const MoeArgs &a, cudaStream_t s)
+{
+    switch (a.H / 256) {
+    case 1: return launch_gateup_nb<1>(a, s);
+    case 2: return launch_gateup_nb<2>(a, s);
+    case 4: return launch_gateup_nb<4>(a, s);
+    case 8: return launch_gateup_nb<8>(a, s);
+    case 16: return launch_gateup_nb<16>(a, s);
+    default: return set_error(BREAD_ERR_ARG, "moe: unsupported H=%d", a.H);
+    }
+}
+
+template <int NB>
+static int launch_down_nb(const MoeArgs &a, cudaStream_t s)
+{
+    using C = K3Cfg<NB>;
+    static bool attr = false;
+    static int per_sm = 1;
+    if (!attr) {
+        BREAD_CUDA(cudaFuncSetAttribute(moe_down_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)C::smem(MOE_TMAX)),
+                   "moe down smem attribute");
+        BREAD_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_down_kernel<NB>, 288, C::smem(1)),
+                   "moe down occupancy");
+        if (per_sm < 1) per_sm = 1;
+        attr = true;
+    }
+    const int items = a.H / MOE_RT3;
+    const int cap = sm_count() * (a.T <= 8 ? per_sm : 1);
+    moe_down_kernel<NB><<<items < cap ? items : cap, 288, C::smem(a.T), s>>>(a);
+    BREAD_CUDA(cudaGetLastError(), "moe down launch");
+    return BREAD_OK;
+}
+
+int moe_launch_down(const MoeArgs &a, cudaStream_t s)
+{
+    switch (a.I / 256) {
+    case 1: return launch_down_nb<1>(a, s);
+    case 2: return launch_down_nb<2>(a, s);
+    case 4: return launch_down_nb<4>(a, s);
+    case 8: return launch_down_nb<8>(a, s);
+    default: return set_error(BREAD_ERR_ARG, "moe: unsupported I=%d", a.I);
+    }
+}
+
+}  // namespace bread
+
+using namespace bread;
+
+extern "C" size_t bread_moe_workspace_bytes(int T, int H, int I, int E, int top_k)
+{
+    if (T < 1 || H < 32 || E < 1 || top_k < 1) return 0;
+    return MoeWs::make(T, H, I, E, top_k).total;
+}
+
+static int moe_prepare(MoeArgs &a, const float *x, const float *W_r, const void *w_sg, int T, int H, int I, int E,
+                       int top_k, void *workspace, size_t workspace_bytes, bool need_experts)
+{
+    BREAD_TRY(moe_check_shapes(T, H, I, E, top_k, need_experts));
+    if (!x || !W_r) return set_error(BREAD_ERR_ARG, "moe: NULL x or W_r");
+    const MoeWs L = MoeWs::make(T, H, need_experts ? I : 0, E, top_k);
+    if (!workspace || workspace_bytes < L.total)
+        return set_error(BREAD_ERR_WORKSPACE, "moe: workspace %zu bytes, need %zu", workspace_bytes, L.total);
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return set_error(BREAD_ERR_ALIGN, "moe: workspace not 256-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(W_r)) & 3)
+        return set_error(BREAD_ERR_ALIGN, "moe: x / W_r not 4-byte aligned");
+    a = MoeArgs{};
+    a.W_r = W_r;
+    a.w_sg = static_cast<const __half *>(w_sg);
+    a.T = T;
+    a.H = H;
+    a.I = I;
+    a.E = E;
+    a.top_k = top_k;
+    a.lo = 0;
+    a.hi = E;
+    a.norm_eps = -1.0f;
+    a.x = x;
+    moe_bind_workspace(a, workspace, L);
+    return BREAD_OK;
+}
+
+extern "C" int bread_moe_route(const float *x, const float *W_r, const void *w_sg, int T, int H, int E, int top_k,
+                               int *idx, float *w, float *sg_weight, void *workspace, size_t workspace_bytes,
+                               cudaStream_t stream)
+{
+    MoeArgs a;
+    BREAD_TRY(moe_prepare(a, x, W_r, w_sg, T, H, 0, E, top_k, workspace, workspace_bytes, false));
+    if (!idx || !w) return set_error(BREAD_ERR_ARG, "moe_route: NULL idx or w");
+    a.idx_out = idx;
+    a.w_out = w;
+    a.sg_out = sg_weight;
+    a.shared_here = 0;
+    BREAD_CUDA(cudaMemsetAsync(a.hdr, 0, 64, stream), "moe_route: reset ticket");
+    return moe_launch_route(a, stream);
+}
+
+extern "C" int bread_moe_ffn(const void *const *gate_ptrs, const void *const *up_ptrs, const void *const *down_ptrs,
+                             const float *W_r, const void *w_sg, const void *sh_gate, const void *sh_up,
+                             const void *sh_down, const float *x, float *out, int T, int H, int I, int E, int top_k,
+                             int *idx_out, float *w_out, float *sg_out, void *workspace, size_t workspace_bytes,
+                             cudaStream_t stream)
+{
+    MoeArgs a;
+    BREAD_TRY(moe_prepare(a, x, W_r, w_sg, T, H, I, E, top_k, workspace, workspace_bytes, true));
+    if (!gate_ptrs || !up_ptrs || !down_ptrs || !out) return set_error(BREAD_ERR_ARG, "moe_ffn: NULL pointer table or out");
+    const int nsh = (sh_gate != nullptr) + (sh_up != nullptr) + (sh_down != nullptr);
+    if (nsh != 0 && nsh != 3) return set_error(BREAD_ERR_ARG, "moe_ffn: give all three shared-expert matrices or none");
+    if (nsh == 3 && ((reinterpret_cast<uintptr_t>(sh_gate) | reinterpret_cast<uintptr_t>(sh_up) |
+                      reinterpret_cast<uintptr_t>(sh_down)) & 15))
+        return set_error(BREAD_ERR_ALIGN, "moe_ffn: shared-expert matrices must be 16-byte aligned");
+    a.gate = reinterpret_cast<const uint8_t *const *>(gate_ptrs);
+    a.up = reinterpret_cast<const uint8_t *const *>(up_ptrs);
+    a.down = reinterpret_cast<const uint8_t *const *>(down_ptrs);
+    a.sh_gate = static_cast<const uint8_t *>(sh_gate);
+    a.sh_up = static_cast<const uint8_t *>(sh_up);
+    a.sh_down = static_cast<const uint8_t *>(sh_down);
+    a.shared_here = nsh == 3;
+    a.out = out;
+    a.idx_out = idx_out;
+    a.w_out = w_out;
+    a.sg_out = sg_out;
+    BREAD_CUDA(cudaMemsetAsync(a.hdr, 0, 64, stream), "moe_ffn: reset ticket");
+    BREAD_TRY(moe_launch_route(a, stream));
+    BREAD_TRY(moe_launch_gateup(a, stream));
+    return moe_launch_down(a, stream);
+}

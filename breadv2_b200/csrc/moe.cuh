@@ -1,0 +1,96 @@
+// moe.cuh -- shared definitions of the MoE FFN kernels (moe.cu) and the stack
+// executor (stack.cu).
+#pragma once
+#include "common.cuh"
+
+namespace bread {
+
+constexpr int MOE_TMAX = 64;     // tokens per call
+constexpr int MOE_EMAX = 512;    // routed experts
+constexpr int MOE_KMAX = 16;     // top-k
+constexpr int MOE_HMAX = 4096;   // hidden size
+constexpr int MOE_IMAX = 2048;   // expert intermediate size
+constexpr int MOE_TC = 8;        // tokens per gate/up work item
+constexpr int MOE_ROWTILE = 32;  // gate/up rows per work item (one activation group)
+constexpr int MOE_RT3 = 16;      // down rows (= output rows) per work item
+
+// Byte offsets of the pieces of a MoE workspace (all 256-byte aligned).
+struct MoeWs {
+    size_t logits, ssq, score, hdr, ridx, rw, sgw, xq, xs, g_expert, g_off, g_cnt, g_cpre, p_token, p_w, aq, as, total;
+    int GM, PM;
+    static MoeWs make(int T, int H, int I, int E, int k)
+    {
+        MoeWs w;
+        size_t o = 0;
+        auto take = [&](size_t bytes) {
+            const size_t at = o;
+            o += (bytes + 255) / 256 * 256;
+            return at;
+        };
+        w.GM = (E < T * k ? E : T * k) + 1;
+        w.PM = T * (k + 1);
+        w.hdr = take(64);
+        w.logits = take((size_t)T * E * 4);
+        w.ssq = take((size_t)T * (H / 32) * 4);
+        w.score = take((size_t)T * 4);
+        w.ridx = take((size_t)T * k * 4);
+        w.rw = take((size_t)T * k * 4);
+        w.sgw = take((size_t)T * 4);
+        w.xq = take((size_t)T * H * 2);
+        w.xs = take((size_t)T * (H / 32) * 4);
+        w.g_expert = take((size_t)w.GM * 4);
+        w.g_off = take((size_t)(w.GM + 1) * 4);
+        w.g_cnt = take((size_t)w.GM * 4);
+        w.g_cpre = take((size_t)(w.GM + 1) * 4);
+        w.p_token = take((size_t)w.PM * 4);
+        w.p_w = take((size_t)w.PM * 4);
+        w.aq = take((size_t)w.PM * (I > 0 ? I : 1) * 2);
+        w.as = take((size_t)w.PM * (I > 0 ? I / 32 : 1) * 4);
+        w.total = o;
+        return w;
+    }
+};
+
+// Header words at MoeWs::hdr.
+enum { HDR_TICKET = 0, HDR_NGROUPS = 1, HDR_NCHUNKS = 2 };
+
+// Everything the three MoE kernels read or write (passed by value).
+struct MoeArgs {
+    const uint8_t *const *gate;  // device tables [E] (routed experts)
+    const uint8_t *const *up;
+    const uint8_t *const *down;
+    const float *W_r;            // [E x H] fp32
+    const __half *w_sg;          // [H] fp16 or NULL
+    const uint8_t *sh_gate, *sh_up, *sh_down;  // shared expert or NULL
+    int T, H, I, E, top_k;
+    int lo, hi;                  // experts computed here: [lo, hi)
+    int shared_here;             // 1: the shared expert is computed here
+    float norm_eps;              // >= 0: inputs are RMS-normalised first
+    const float *x;              // router / expert input [T x H]
+    float *out;                  // [T x H] accumulated into
+    // workspace
+    int *hdr;
+    float *logits, *ssq, *score;
+    int *ridx;
+    float *rw, *sgw;
+    int16_t *xq;
+    float *xs;
+    int *g_expert, *g_off, *g_cnt, *g_cpre, *p_token;
+    float *p_w;
+    int16_t *aq;
+    float *as;
+    // optional routing copies
+    int *idx_out;
+    float *w_out, *sg_out;
+    int *stats;  // optional: [groups, pairs] computed here (written by K1)
+};
+
+void moe_bind_workspace(MoeArgs &a, void *ws, const MoeWs &L);
+int moe_check_shapes(int T, int H, int I, int E, int top_k, bool need_experts);
+// K1 (router + finalize), K2 (gate/up + SiLU*mul), K3 (down + combine).
+int moe_launch_route(const MoeArgs &a, cudaStream_t s);
+int moe_launch_gateup(const MoeArgs &a, cudaStream_t s);
+int moe_launch_down(const MoeArgs &a, cudaStream_t s);
+int moe_route_grid(const MoeArgs &a);
+
+}  // namespace bread

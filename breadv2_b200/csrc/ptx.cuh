@@ -1,0 +1,125 @@
+// ptx.cuh -- inline-PTX helpers for sm_100a: mbarriers, 1-D bulk async copies
+// (TMA, no multicast), bounded waits, integer dot products, exact small-int
+// to float conversions.
+#pragma once
+#include <stdint.h>
+#include "common.cuh"
+
+namespace bread {
+
+// Device-wide error word (bits DEVERR_*), read by bread_device_error().
+extern __device__ unsigned g_dev_error;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void flag_error(unsigned bit) { atomicOr(&g_dev_error, bit); }
+
+// ---- mbarrier -------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// Make barrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_mbar_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, unsigned bytes)
+{
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                     smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for phase `parity` of `bar` to complete, at most SPIN_LIMIT polls.
+// Returns false (and sets the device error word) when the budget runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    for (long long i = 0; i < SPIN_LIMIT; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (i > 64) __nanosleep(64);
+    }
+    flag_error(DEVERR_TIMEOUT);
+    return false;
+}
+
+// ---- 1-D bulk copy global -> shared (TMA engine, no multicast) ------------
+// dst and src 16-byte aligned, bytes a multiple of 16.  Completion is counted
+// on `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+// Order this thread's generic-proxy shared-memory accesses before later
+// async-proxy (bulk copy) accesses of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- named barrier for a subset of warps -----------------------------------
+__device__ __forceinline__ void named_sync(int id, int threads)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---- programmatic dependent launch ---------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ---- integer dot products ---------------------------------------------------
+// a: two signed 16-bit values; b: four unsigned bytes.  lo uses bytes 0,1 of
+// b, hi uses bytes 2,3:  c + a.h0*b.byte(0|2) + a.h1*b.byte(1|3).  Exact.
+__device__ __forceinline__ int dp2a_lo(int a, unsigned b, int c)
+{
+    int d;
+    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp2a_hi(int a, unsigned b, int c)
+{
+    int d;
+    asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// Sum of the two signed 16-bit halves of a, plus c.
+__device__ __forceinline__ int sum_i16x2(int a, int c) { return dp2a_lo(a, 0x0101u, c); }
+
+// ---- exact small integer -> float ------------------------------------------
+// For 0 <= u < 2^23: the float with bit pattern 0x4B000000|u is 2^23 + u, so
+// subtracting 2^23 is exact.
+__device__ __forceinline__ float u2f_small(uint32_t u)
+{
+    return __int_as_float(0x4B000000 | u) - 8388608.0f;
+}
+// For |s| < 2^22: 0x4B400000 is 1.5*2^23; adding s to the pattern adds s to
+// the value, exactly.
+__device__ __forceinline__ float s2f_small(int s)
+{
+    return __int_as_float(0x4B400000 + s) - 12582912.0f;
+}
+
+}  // namespace bread

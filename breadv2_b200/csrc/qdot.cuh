@@ -1,0 +1,279 @@
+// qdot.cuh -- Q4_K / Q6_K / Q8_0 decoding on sm_100a.
+//
+// Two families of device functions:
+//   * exact element dequantisation (the arithmetic of the reference CPU
+//     decoders layer_ops.cu:44-105, each product rounded separately), used by
+//     bread_dequant and by the alignment-agnostic GEMV;
+//   * "lane dots": one lane's share of a super-block row dot product against
+//     an activation slice quantised to 16-bit fixed point per 32 values.  The
+//     weight side stays exact: per sub-block the reference weight is
+//     d*sc*q - dmin*m (Q4_K) or d*sc*(q-32) (Q6_K), so
+//         sum_i w_i x_i = d*sc*s_x*SUM(q_i xq_i) - dmin*m*s_x*SUM(xq_i)
+//     where xq_i = round(x_i / s_x) and the inner SUMs are exact int32 dot
+//     products (dp2a).  The only approximation is x ~= s_x*xq
+//     (|error| <= s_x/2 = max|x_group| / 65534).
+#pragma once
+#include <stdint.h>
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace bread {
+
+// ---------------------------------------------------------------------------
+// exact dequantisation (reference layer_ops.cu:44-105, kernels.cu:251-284)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float h2f_bits(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+
+__device__ __forceinline__ void q4k_scale_min(const uint8_t *s, int j, int &sc, int &m)
+{
+    if (j < 4) {
+        sc = s[j] & 63;
+        m = s[j + 4] & 63;
+    } else {
+        sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+        m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+// Element e (0..255) of a Q4_K block: (d*sc)*q - (dmin*m), no FMA.
+__device__ __forceinline__ float q4k_elem_exact(const uint8_t *blk, int e)
+{
+    const float d = h2f_bits((uint16_t)(blk[0] | (blk[1] << 8)));
+    const float dmin = h2f_bits((uint16_t)(blk[2] | (blk[3] << 8)));
+    const int grp = e >> 6, sub = (e >> 5) & 1, pos = e & 31;
+    int sc, m;
+    q4k_scale_min(blk + 4, 2 * grp + sub, sc, m);
+    const uint8_t qb = blk[16 + 32 * grp + pos];
+    const int q = sub ? (qb >> 4) : (qb & 0xF);
+    const float d1 = __fmul_rn(d, (float)sc);
+    const float m1 = __fmul_rn(dmin, (float)m);
+    return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+}
+
+// Element e of a Q6_K block: (d*sc)*(q-32), left to right, no FMA.
+__device__ __forceinline__ float q6k_elem_exact(const uint8_t *blk, int e)
+{
+    const float d = h2f_bits((uint16_t)(blk[208] | (blk[209] << 8)));
+    const int half = e >> 7, r = (e >> 5) & 3, l = e & 31;
+    const uint8_t *ql = blk + 64 * half, *qh = blk + 128 + 32 * half;
+    const int8_t *sc = (const int8_t *)(blk + 192 + 8 * half);
+    const uint8_t qlb = ql[l + 32 * (r & 1)];
+    const int lo4 = (r >> 1) ? (qlb >> 4) : (qlb & 0xF);
+    const int hi2 = (qh[l] >> (2 * r)) & 3;
+    const int q = (lo4 | (hi2 << 4)) - 32;
+    return __fmul_rn(__fmul_rn(d, (float)sc[l / 16 + 2 * r]), (float)q);
+}
+
+// Element e (0..31) of a Q8_0 block: d*q.
+__device__ __forceinline__ float q80_elem_exact(const uint8_t *blk, int e)
+{
+    const float d = h2f_bits((uint16_t)(blk[0] | (blk[1] << 8)));
+    return __fmul_rn(d, (float)(int8_t)blk[2 + e]);
+}
+
+template <int QT>
+__device__ __forceinline__ float elem_exact(const uint8_t *blk, int e)
+{
+    if (QT == BREAD_QTYPE_Q4_K) return q4k_elem_exact(blk, e);
+    if (QT == BREAD_QTYPE_Q6_K) return q6k_elem_exact(blk, e);
+    return q80_elem_exact(blk, e);
+}
+
+// ---------------------------------------------------------------------------
+// activation quantisation: 32 values -> int16 + one fp32 scale
+// ---------------------------------------------------------------------------
+// Called by a full warp with one value per lane; returns the lane's int16 and
+// writes the group scale (max|x| / 32767) to *scale on lane 0.  An all-zero
+// group gets scale 0; a non-finite value gives a NaN scale (outputs NaN).
+__device__ __forceinline__ int quant32(float v, float *scale, int lane)
+{
+    float a = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    const bool finite = a <= 3.402823466e38f;  // false for inf and NaN
+    a = __shfl_sync(0xffffffffu, finite ? a : __int_as_float(0x7fc00000), 0);
+    int q = 0;
+    if (a > 0.0f && finite) q = __float2int_rn((v / a) * 32767.0f);  // |v/a| <= 1, also for subnormal a
+    if (lane == 0) *scale = finite ? a * (1.0f / 32767.0f) : __int_as_float(0x7fc00000);
+    return q;
+}
+
+// ---------------------------------------------------------------------------
+// lane dots
+// ---------------------------------------------------------------------------
+// One lane's activation slice for one token: 64 int16 (two per int).
+struct XSlice {
+    int v[32];
+    float s[4];
+    int c[4];
+};
+
+// Q4_K lane (block b, pair g): block elements 64g..64g+63, i.e. sub-blocks 2g
+// (low nibbles of qs[32g..32g+31]) and 2g+1 (high nibbles).
+// xq/xs: the token's int16 values and per-32 scales; e0 = 256*b + 64*g.
+__device__ __forceinline__ void load_slice_q4k(XSlice &X, const int16_t *xq, const float *xs, int e0)
+{
+    const int4 *p = reinterpret_cast<const int4 *>(xq + e0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int4 t = p[i];
+        X.v[4 * i + 0] = t.x;
+        X.v[4 * i + 1] = t.y;
+        X.v[4 * i + 2] = t.z;
+        X.v[4 * i + 3] = t.w;
+    }
+    int s0 = 0, s1 = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        s0 = sum_i16x2(X.v[i], s0);
+        s1 = sum_i16x2(X.v[16 + i], s1);
+    }
+    const float f0 = xs[e0 >> 5], f1 = xs[(e0 >> 5) + 1];
+    X.s[0] = f0;
+    X.s[1] = f1 * 0.0625f;  // the high nibbles enter the dot product as 16*q
+    X.s[2] = f0 * (float)s0;
+    X.s[3] = f1 * (float)s1;
+}
+
+// blk: 16-byte aligned Q4_K block; g: 0..3.
+__device__ __forceinline__ float q4k_lane_dot(const uint8_t *blk, int g, const XSlice &X)
+{
+    const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
+    const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * g);
+    const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    int p0 = 0, p1 = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = w[i] & 0xF0F0F0F0u;
+        p0 = dp2a_lo(X.v[2 * i], lo, p0);
+        p0 = dp2a_hi(X.v[2 * i + 1], lo, p0);
+        p1 = dp2a_lo(X.v[16 + 2 * i], hi, p1);
+        p1 = dp2a_hi(X.v[16 + 2 * i + 1], hi, p1);
+    }
+    // (scale, min) of sub-blocks 2g and 2g+1 from the 12 packed bytes, both at
+    // once (two bytes per field), following dequant_q4k_cpu.c:70-79.
+    const uint32_t sh = 16u * (uint32_t)(g & 1);
+    const uint32_t A = hd.y >> sh, B = hd.z >> sh, C = hd.w >> sh;
+    uint32_t scp, mp;
+    if (g >= 2) {
+        scp = (C & 0x0F0Fu) | ((A >> 2) & 0x3030u);
+        mp = ((C >> 4) & 0x0F0Fu) | ((B >> 2) & 0x3030u);
+    } else {
+        scp = A & 0x3F3Fu;
+        mp = B & 0x3F3Fu;
+    }
+    const float sc0 = u2f_small(scp & 0xFFu), sc1 = u2f_small((scp >> 8) & 0xFFu);
+    const float m0 = u2f_small(mp & 0xFFu), m1 = u2f_small((mp >> 8) & 0xFFu);
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&hd.x));
+    const float u = fmaf(sc1 * X.s[1], (float)p1, (sc0 * X.s[0]) * (float)p0);
+    const float mm = fmaf(m1, X.s[3], m0 * X.s[2]);
+    return fmaf(dd.x, u, -dd.y * mm);
+}
+
+// Q6_K lane (block b, half h, l-group g): block elements 128h + 32r + 16g + i
+// for r = 0..3, i = 0..15 (four runs of 16).  base = 256*b + 128*h.
+__device__ __forceinline__ void load_slice_q6k(XSlice &X, const int16_t *xq, const float *xs, int base, int g)
+{
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int4 *p = reinterpret_cast<const int4 *>(xq + base + 32 * r + 16 * g);
+        const int4 t0 = p[0], t1 = p[1];
+        X.v[8 * r + 0] = t0.x;
+        X.v[8 * r + 1] = t0.y;
+        X.v[8 * r + 2] = t0.z;
+        X.v[8 * r + 3] = t0.w;
+        X.v[8 * r + 4] = t1.x;
+        X.v[8 * r + 5] = t1.y;
+        X.v[8 * r + 6] = t1.z;
+        X.v[8 * r + 7] = t1.w;
+        int s = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s = sum_i16x2(X.v[8 * r + i], s);
+        X.c[r] = 32 * s;
+        X.s[r] = xs[(base >> 5) + r];
+    }
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel)
+{
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// 16 bytes at p (2-byte aligned; sh = p & 3, sel = sh ? 0x5432 : 0x3210)
+// from 4-byte aligned shared-memory words.
+__device__ __forceinline__ void ld16_shift(const uint8_t *p, int sh, uint32_t sel, uint32_t o[4])
+{
+    const uint32_t *q = reinterpret_cast<const uint32_t *>(p - sh);
+    const uint32_t w0 = q[0], w1 = q[1], w2 = q[2], w3 = q[3], w4 = q[4];
+    o[0] = prmt(w0, w1, sel);
+    o[1] = prmt(w1, w2, sel);
+    o[2] = prmt(w2, w3, sel);
+    o[3] = prmt(w3, w4, sel);
+}
+
+// Per-lane constants of a Q6_K lane: byte shift of its block, permute
+// selector, and the four sign-extending selectors picking int8 scales
+// g, g+2 (of scales 0..3 of the half) and g, g+2 (of scales 4..7).
+struct Q6Lane {
+    int sh;
+    uint32_t sel;
+    uint32_t ssel[2];
+};
+__device__ __forceinline__ uint32_t sext_sel(int k)
+{
+    const uint32_t s = (uint32_t)(k | 8);
+    return (uint32_t)k | (s << 4) | (s << 8) | (s << 12);
+}
+__device__ __forceinline__ Q6Lane q6_lane(int sh, int g)
+{
+    Q6Lane L;
+    L.sh = sh;
+    L.sel = sh ? 0x5432u : 0x3210u;
+    L.ssel[0] = sext_sel(g);
+    L.ssel[1] = sext_sel(g + 2);
+    return L;
+}
+
+// blk: Q6_K block in shared memory (2-byte aligned, (blk & 3) == L.sh).
+__device__ __forceinline__ float q6k_lane_dot(const uint8_t *blk, int h, int g, const Q6Lane &L, const XSlice &X)
+{
+    uint32_t A[4], B[4], Q[4];
+    ld16_shift(blk + 64 * h + 16 * g, L.sh, L.sel, A);
+    ld16_shift(blk + 64 * h + 32 + 16 * g, L.sh, L.sel, B);
+    ld16_shift(blk + 128 + 32 * h + 16 * g, L.sh, L.sel, Q);
+    int p0 = 0, p1 = 0, p2 = 0, p3 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        // 6-bit values of l = 16g+4i..+3 for runs r = 0..3 (dequant_q4k_cpu.c:157-160)
+        const uint32_t v0 = (A[i] & 0x0F0F0F0Fu) | ((Q[i] << 4) & 0x30303030u);
+        const uint32_t v1 = (B[i] & 0x0F0F0F0Fu) | ((Q[i] << 2) & 0x30303030u);
+        const uint32_t v2 = ((A[i] >> 4) & 0x0F0F0F0Fu) | (Q[i] & 0x30303030u);
+        const uint32_t v3 = ((B[i] >> 4) & 0x0F0F0F0Fu) | ((Q[i] >> 2) & 0x30303030u);
+        p0 = dp2a_lo(X.v[2 * i], v0, p0);
+        p0 = dp2a_hi(X.v[2 * i + 1], v0, p0);
+        p1 = dp2a_lo(X.v[8 + 2 * i], v1, p1);
+        p1 = dp2a_hi(X.v[8 + 2 * i + 1], v1, p1);
+        p2 = dp2a_lo(X.v[16 + 2 * i], v2, p2);
+        p2 = dp2a_hi(X.v[16 + 2 * i + 1], v2, p2);
+        p3 = dp2a_lo(X.v[24 + 2 * i], v3, p3);
+        p3 = dp2a_hi(X.v[24 + 2 * i + 1], v3, p3);
+    }
+    const uint32_t *sq = reinterpret_cast<const uint32_t *>(blk + 192 + 8 * h - L.sh);
+    const uint32_t w0 = sq[0], w1 = sq[1], w2 = sq[2];
+    const uint32_t slo = prmt(w0, w1, L.sel), shi = prmt(w1, w2, L.sel);
+    const int sc0 = (int)prmt(slo, 0u, L.ssel[0]);
+    const int sc1 = (int)prmt(slo, 0u, L.ssel[1]);
+    const int sc2 = (int)prmt(shi, 0u, L.ssel[0]);
+    const int sc3 = (int)prmt(shi, 0u, L.ssel[1]);
+    float acc = (s2f_small(sc0) * X.s[0]) * (float)(p0 - X.c[0]);
+    acc = fmaf(s2f_small(sc1) * X.s[1], (float)(p1 - X.c[1]), acc);
+    acc = fmaf(s2f_small(sc2) * X.s[2], (float)(p2 - X.c[2]), acc);
+    acc = fmaf(s2f_small(sc3) * X.s[3], (float)(p3 - X.c[3]), acc);
+    const float d = __half2float(*reinterpret_cast<const __half *>(blk + 208));
+    return d * acc;
+}
+
+}  // namespace bread

@@ -1,0 +1,458 @@
+/* oracle.c -- CPU restatement of BREAD's quantised-expert MoE path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker for the CUDA
+ * library in breadv2_b200/.  Only tests/, __graft_entry__.smoke() and the
+ * CPU-baseline leg of bench.py may load it; nothing on the product path
+ * calls it.
+ *
+ * Every function names the reference routine (path inside arahe-dev/breadv2)
+ * whose arithmetic it restates.  The restatement is pinned two ways:
+ *   - against the reference's own known-answer blocks (dequant_q4k_cpu.c:181-283);
+ *   - against the reference's own CPU code compiled from its sources into
+ *     oracle/_ref/ (see oracle/Makefile), via the fixtures in tests/golden/.
+ *
+ * Build: gcc -O2 -ffp-contract=off (no FMA contraction: the reference's x86-64
+ * host code computes every product and sum as separately rounded fp32 ops).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define ORC_QK 256
+#define ORC_Q4K_BYTES 144
+#define ORC_Q6K_BYTES 210
+#define ORC_Q80_BYTES 34
+#define ORC_Q80_ELEMS 32
+
+#define ORC_Q8_0 8
+#define ORC_Q4_K 12
+#define ORC_Q6_K 14
+
+/* ------------------------------------------------------------------ */
+/* fp16 -> fp32                                                        */
+/* ------------------------------------------------------------------ */
+
+/* Exact IEEE half decode, subnormals included: bread_utils.h:27-47
+ * (bread_h2f), which layer_ops.cu:52-53,85 use.  Subnormal value is
+ * mantissa * 2^-24. */
+float orc_h2f(uint16_t h)
+{
+    uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t ex = (h >> 10) & 0x1Fu;
+    uint32_t man = h & 0x3FFu;
+    uint32_t bits;
+    float f;
+    if (ex == 0) {
+        float v = (float)man * (1.0f / 16777216.0f);
+        return (h >> 15) ? -v : v;
+    }
+    if (ex == 31) bits = sign | 0x7F800000u | (man << 13);
+    else bits = sign | ((ex + 112u) << 23) | (man << 13);
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* Flush-to-zero decode of dequant_q4k_cpu.c:38-56 (fp16_to_fp32): a zero
+ * exponent gives a signed zero, so subnormal scales decode to 0. */
+float orc_h2f_ftz(uint16_t h)
+{
+    uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t ex = (h >> 10) & 0x1Fu;
+    uint32_t man = h & 0x3FFu;
+    uint32_t bits;
+    float f;
+    if (ex == 0) bits = sign;
+    else if (ex == 31) bits = sign | 0x7F800000u | (man << 13);
+    else bits = sign | ((ex + 112u) << 23) | (man << 13);
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* fp32 -> fp16, round to nearest even (used only to build fp16 test inputs
+ * and to mimic the reference's fp16 output rounding, kernels.cu:191). */
+uint16_t orc_f2h(float f)
+{
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t ex = (x >> 23) & 0xFFu;
+    uint32_t man = x & 0x7FFFFFu;
+    if (ex == 0xFF) return (uint16_t)(sign | 0x7C00u | (man ? 0x200u : 0u));
+    int e = (int)ex - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7C00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        man |= 0x800000u;
+        int shift = 14 - e;
+        uint32_t half_bit = 1u << (shift - 1);
+        uint32_t rest = man & ((1u << shift) - 1u);
+        uint32_t r = man >> shift;
+        if (rest > half_bit || (rest == half_bit && (r & 1u))) r++;
+        return (uint16_t)(sign | r);
+    }
+    uint32_t r = ((uint32_t)e << 10) | (man >> 13);
+    uint32_t rest = man & 0x1FFFu;
+    if (rest > 0x1000u || (rest == 0x1000u && (r & 1u))) r++;
+    return (uint16_t)(sign | r);
+}
+
+/* ------------------------------------------------------------------ */
+/* Block dequantisation                                                */
+/* ------------------------------------------------------------------ */
+
+/* 6-bit (scale, min) pair j of the 12 packed bytes:
+ * dequant_q4k_cpu.c:70-79 / layer_ops.cu:32-42. */
+static void orc_scale_min_k4(int j, const uint8_t *s, int *sc, int *m)
+{
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *m = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4);
+        *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+/* One 144-byte Q4_K super-block -> 256 floats.
+ * layer_ops.cu:44-75 (ftz=0) and dequant_q4k_cpu.c:90-123 (ftz=1).
+ * Rounding: d1 = d*sc, m1 = dmin*m, y = d1*q - m1, each op rounded. */
+void orc_dequant_q4k_block(const uint8_t *blk, float *out, int ftz)
+{
+    uint16_t dr, mr;
+    memcpy(&dr, blk, 2);
+    memcpy(&mr, blk + 2, 2);
+    const float d = ftz ? orc_h2f_ftz(dr) : orc_h2f(dr);
+    const float dmin = ftz ? orc_h2f_ftz(mr) : orc_h2f(mr);
+    const uint8_t *scales = blk + 4;
+    const uint8_t *q = blk + 16;
+    for (int g = 0; g < 4; g++) {
+        int sc, m;
+        orc_scale_min_k4(2 * g, scales, &sc, &m);
+        const float d1 = d * (float)sc;
+        const float m1 = dmin * (float)m;
+        orc_scale_min_k4(2 * g + 1, scales, &sc, &m);
+        const float d2 = d * (float)sc;
+        const float m2 = dmin * (float)m;
+        for (int l = 0; l < 32; l++) out[64 * g + l] = d1 * (float)(q[l] & 0xF) - m1;
+        for (int l = 0; l < 32; l++) out[64 * g + 32 + l] = d2 * (float)(q[l] >> 4) - m2;
+        q += 32;
+    }
+}
+
+/* One 210-byte Q6_K super-block -> 256 floats.
+ * layer_ops.cu:77-105 (ftz=0) and dequant_q4k_cpu.c:141-172 (ftz=1).
+ * y = (d*sc)*q, left to right, each product rounded. */
+void orc_dequant_q6k_block(const uint8_t *blk, float *out, int ftz)
+{
+    uint16_t dr;
+    memcpy(&dr, blk + 208, 2);
+    const float d = ftz ? orc_h2f_ftz(dr) : orc_h2f(dr);
+    const uint8_t *ql = blk;
+    const uint8_t *qh = blk + 128;
+    const int8_t *sc = (const int8_t *)(blk + 192);
+    for (int half = 0; half < 2; half++) {
+        for (int l = 0; l < 32; l++) {
+            const int is = l / 16;
+            const int q1 = (int)((ql[l] & 0xF) | (((qh[l] >> 0) & 3) << 4)) - 32;
+            const int q2 = (int)((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+            const int q3 = (int)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+            const int q4 = (int)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+            out[128 * half + l] = d * (float)sc[is + 0] * (float)q1;
+            out[128 * half + l + 32] = d * (float)sc[is + 2] * (float)q2;
+            out[128 * half + l + 64] = d * (float)sc[is + 4] * (float)q3;
+            out[128 * half + l + 96] = d * (float)sc[is + 6] * (float)q4;
+        }
+        ql += 64;
+        qh += 32;
+        sc += 8;
+    }
+}
+
+/* One 34-byte Q8_0 block -> 32 floats: w = d * q (kernels.cu:251-284). */
+void orc_dequant_q8_0_block(const uint8_t *blk, float *out)
+{
+    uint16_t dr;
+    memcpy(&dr, blk, 2);
+    const float d = orc_h2f(dr);
+    const int8_t *q = (const int8_t *)(blk + 2);
+    for (int i = 0; i < ORC_Q80_ELEMS; i++) out[i] = d * (float)q[i];
+}
+
+static int orc_block_elems(int qtype) { return qtype == ORC_Q8_0 ? ORC_Q80_ELEMS : ORC_QK; }
+static int orc_block_bytes(int qtype)
+{
+    switch (qtype) {
+    case ORC_Q4_K: return ORC_Q4K_BYTES;
+    case ORC_Q6_K: return ORC_Q6K_BYTES;
+    case ORC_Q8_0: return ORC_Q80_BYTES;
+    default: return 0;
+    }
+}
+
+static void orc_dequant_block(const uint8_t *blk, int qtype, float *out, int ftz)
+{
+    if (qtype == ORC_Q4_K) orc_dequant_q4k_block(blk, out, ftz);
+    else if (qtype == ORC_Q6_K) orc_dequant_q6k_block(blk, out, ftz);
+    else orc_dequant_q8_0_block(blk, out);
+}
+
+/* n_blocks consecutive blocks -> n_blocks*block_elems floats.  Returns -1 on
+ * an unknown qtype. */
+int orc_dequant(const uint8_t *w, int qtype, long long n_blocks, float *out, int ftz)
+{
+    const int bb = orc_block_bytes(qtype), be = orc_block_elems(qtype);
+    if (!bb) return -1;
+    for (long long b = 0; b < n_blocks; b++)
+        orc_dequant_block(w + b * bb, qtype, out + b * be, ftz);
+    return 0;
+}
+
+/* ------------------------------------------------------------------ */
+/* Matrix-vector products                                              */
+/* ------------------------------------------------------------------ */
+
+/* fp32 sequential sum, the reference CPU GEMV: layer_ops.cu:133-167
+ * (cpu_matvec_q4k / cpu_matvec_q6k): per row, dequantise each block then
+ * sum += w[i]*x[i] in column order, one fp32 accumulator. */
+int orc_matvec_f32(const uint8_t *w, int qtype, const float *x, float *y, int rows, int cols)
+{
+    const int bb = orc_block_bytes(qtype), be = orc_block_elems(qtype);
+    if (!bb || cols % be) return -1;
+    const int nb = cols / be;
+    float blk[ORC_QK];
+    for (int r = 0; r < rows; r++) {
+        const uint8_t *row = w + (size_t)r * nb * bb;
+        float sum = 0.0f;
+        for (int b = 0; b < nb; b++) {
+            orc_dequant_block(row + (size_t)b * bb, qtype, blk, 0);
+            for (int i = 0; i < be; i++) sum += blk[i] * x[b * be + i];
+        }
+        y[r] = sum;
+    }
+    return 0;
+}
+
+/* fp64-accumulated GEMV of the exactly dequantised weights: the reference
+ * result the 1e-3 relative-L2 bar is measured against.  x is fp32 (T rows of
+ * cols), y is fp64 (T rows of `rows`). */
+int orc_matvec_f64(const uint8_t *w, int qtype, const float *x, double *y, int rows, int cols, int T)
+{
+    const int bb = orc_block_bytes(qtype), be = orc_block_elems(qtype);
+    if (!bb || cols % be) return -1;
+    const int nb = cols / be;
+    float blk[ORC_QK];
+    for (int r = 0; r < rows; r++) {
+        const uint8_t *row = w + (size_t)r * nb * bb;
+        for (int t = 0; t < T; t++) y[(size_t)t * rows + r] = 0.0;
+        for (int b = 0; b < nb; b++) {
+            orc_dequant_block(row + (size_t)b * bb, qtype, blk, 0);
+            for (int t = 0; t < T; t++) {
+                const float *xt = x + (size_t)t * cols + b * be;
+                double s = 0.0;
+                for (int i = 0; i < be; i++) s += (double)blk[i] * (double)xt[i];
+                y[(size_t)t * rows + r] += s;
+            }
+        }
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------------ */
+/* Routing: one_layer.cu:937-992 (route_layer) with layer_ops.cu:222-250  */
+/* ------------------------------------------------------------------ */
+
+/* cpu_softmax, layer_ops.cu:222-229 */
+void orc_softmax(float *x, int n)
+{
+    float mx = x[0];
+    for (int i = 1; i < n; i++) if (x[i] > mx) mx = x[i];
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) { x[i] = expf(x[i] - mx); s += x[i]; }
+    for (int i = 0; i < n; i++) x[i] /= s;
+}
+
+/* cpu_topk, layer_ops.cu:231-250: K rounds of argmax with a strict '>', so
+ * the lowest index wins a tie; weights renormalised to sum to one. */
+void orc_topk(const float *p, int n, int K, int *idx, float *wt)
+{
+    unsigned char used[4096];
+    memset(used, 0, (size_t)n);
+    float wsum = 0.0f;
+    for (int k = 0; k < K; k++) {
+        int best = -1;
+        float bv = -1e30f;
+        for (int i = 0; i < n; i++)
+            if (!used[i] && p[i] > bv) { bv = p[i]; best = i; }
+        idx[k] = best;
+        wt[k] = bv;
+        wsum += bv;
+        used[best] = 1;
+    }
+    if (wsum > 0.0f)
+        for (int k = 0; k < K; k++) wt[k] /= wsum;
+}
+
+/* route_layer for T tokens.  logits[e] = sum_j W_r[e*H+j]*x[j] in fp32,
+ * j ascending (one_layer.cu:969-971); shared-gate score = sum_j
+ * f16(w_sg[j])*x[j] (one_layer.cu:973-980), 0 when w_sg is NULL; then softmax
+ * and top-k.  sg_weight[t] = sigmoid(score) = 1/(1+expf(-score))
+ * (layer_ops.cu:252-255, applied at one_layer.cu:1889).  logits_out (T*E)
+ * receives the raw logits when non-NULL. */
+int orc_route(const float *x, const float *W_r, const uint16_t *w_sg, int T, int H, int E, int top_k,
+              int *idx, float *wt, float *sg_weight, float *logits_out)
+{
+    if (E > 4096 || top_k > E) return -1;
+    float *lg = (float *)malloc((size_t)E * sizeof(float));
+    if (!lg) return -2;
+    for (int t = 0; t < T; t++) {
+        const float *xt = x + (size_t)t * H;
+        for (int e = 0; e < E; e++) {
+            float acc = 0.0f;
+            for (int j = 0; j < H; j++) acc += W_r[(size_t)e * H + j] * xt[j];
+            lg[e] = acc;
+        }
+        if (logits_out) memcpy(logits_out + (size_t)t * E, lg, (size_t)E * sizeof(float));
+        float score = 0.0f;
+        if (w_sg)
+            for (int j = 0; j < H; j++) score += orc_h2f(w_sg[j]) * xt[j];
+        sg_weight[t] = 1.0f / (1.0f + expf(-score));
+        orc_softmax(lg, E);
+        orc_topk(lg, E, top_k, idx + (size_t)t * top_k, wt + (size_t)t * top_k);
+    }
+    free(lg);
+    return 0;
+}
+
+/* fp64 logits, for measuring how far the k-th and (k+1)-th choices are
+ * apart (a routing decision is only defined to fp32 summation noise). */
+void orc_router_logits_f64(const float *x, const float *W_r, int T, int H, int E, double *out)
+{
+    for (int t = 0; t < T; t++)
+        for (int e = 0; e < E; e++) {
+            double acc = 0.0;
+            for (int j = 0; j < H; j++) acc += (double)W_r[(size_t)e * H + j] * (double)x[(size_t)t * H + j];
+            out[(size_t)t * E + e] = acc;
+        }
+}
+
+/* ------------------------------------------------------------------ */
+/* Expert FFN                                                          */
+/* ------------------------------------------------------------------ */
+
+/* cpu_swiglu, layer_ops.cu:214-220: out = (g/(1+expf(-g)))*u */
+void orc_swiglu(const float *g, const float *u, float *out, int n)
+{
+    for (int i = 0; i < n; i++) {
+        const float gv = g[i];
+        out[i] = (gv / (1.0f + expf(-gv))) * u[i];
+    }
+}
+
+/* One expert (or the shared expert) in fp64 for token x (fp32[H]):
+ * gate/up Q4_K [I x H], down Q6_K [H x I]; out[H] += w * down(silu(gate x) * (up x)).
+ * Mirrors the per-expert body of the expert loop, one_layer.cu:1966-1981
+ * (gate, up, silu*mul, down, scale_accum), with every sum in fp64. */
+static void orc_expert_f64(const uint8_t *gate, const uint8_t *up, const uint8_t *down, const float *x, int H, int I,
+                           double w, double *out, double *gb, double *ub)
+{
+    orc_matvec_f64(gate, ORC_Q4_K, x, gb, I, H, 1);
+    orc_matvec_f64(up, ORC_Q4_K, x, ub, I, H, 1);
+    for (int i = 0; i < I; i++) {
+        const double g = gb[i];
+        gb[i] = (g / (1.0 + exp(-g))) * ub[i];
+    }
+    /* down projection with an fp64 activation: dequantised rows in fp32
+     * (exact), products and sums in fp64 */
+    const int nb = I / ORC_QK;
+    float blk[ORC_QK];
+    for (int r = 0; r < H; r++) {
+        const uint8_t *row = down + (size_t)r * nb * ORC_Q6K_BYTES;
+        double s = 0.0;
+        for (int b = 0; b < nb; b++) {
+            orc_dequant_q6k_block(row + (size_t)b * ORC_Q6K_BYTES, blk, 0);
+            for (int i = 0; i < ORC_QK; i++) s += (double)blk[i] * gb[b * ORC_QK + i];
+        }
+        out[r] += w * s;
+    }
+}
+
+/* MoE FFN of T tokens in fp64, given the routing: for each token,
+ * out[t] = sum_k wt[t,k] * expert_{idx[t,k]}(x_t) + sg_weight[t] * shared(x_t).
+ * gate_ptrs/up_ptrs/down_ptrs index experts by id (host pointers).  shared_*
+ * may be NULL (no shared expert).  out is fp64 [T x H], overwritten. */
+int orc_moe_f64(const uint8_t *const *gate_ptrs, const uint8_t *const *up_ptrs, const uint8_t *const *down_ptrs,
+                const uint8_t *sh_gate, const uint8_t *sh_up, const uint8_t *sh_down, const float *x,
+                const int *idx, const float *wt, const float *sg_weight, int T, int H, int I, int top_k, double *out)
+{
+    double *gb = (double *)malloc((size_t)I * sizeof(double));
+    double *ub = (double *)malloc((size_t)I * sizeof(double));
+    if (!gb || !ub) return -2;
+    for (int t = 0; t < T; t++) {
+        double *o = out + (size_t)t * H;
+        const float *xt = x + (size_t)t * H;
+        for (int r = 0; r < H; r++) o[r] = 0.0;
+        for (int k = 0; k < top_k; k++) {
+            const int e = idx[(size_t)t * top_k + k];
+            orc_expert_f64(gate_ptrs[e], up_ptrs[e], down_ptrs[e], xt, H, I, (double)wt[(size_t)t * top_k + k], o, gb,
+                           ub);
+        }
+        if (sh_gate && sh_up && sh_down)
+            orc_expert_f64(sh_gate, sh_up, sh_down, xt, H, I, (double)sg_weight[t], o, gb, ub);
+    }
+    free(gb);
+    free(ub);
+    return 0;
+}
+
+/* The reference's fp32 expert block, structured as expert_bench.cu:158-179:
+ * per expert gate/up GEMV (fp32 sequential), swiglu, down GEMV, scale by the
+ * routing weight, then a serial sum over experts in k order; the shared expert
+ * follows as in one_layer.cu:1871-1891.  out fp32 [T x H], overwritten. */
+int orc_moe_f32(const uint8_t *const *gate_ptrs, const uint8_t *const *up_ptrs, const uint8_t *const *down_ptrs,
+                const uint8_t *sh_gate, const uint8_t *sh_up, const uint8_t *sh_down, const float *x,
+                const int *idx, const float *wt, const float *sg_weight, int T, int H, int I, int top_k, float *out)
+{
+    float *g = (float *)malloc((size_t)I * sizeof(float));
+    float *u = (float *)malloc((size_t)I * sizeof(float));
+    float *o = (float *)malloc((size_t)H * sizeof(float));
+    if (!g || !u || !o) return -2;
+    for (int t = 0; t < T; t++) {
+        float *ot = out + (size_t)t * H;
+        const float *xt = x + (size_t)t * H;
+        for (int r = 0; r < H; r++) ot[r] = 0.0f;
+        for (int k = 0; k <= top_k; k++) {
+            const uint8_t *wg, *wu, *wd;
+            float w;
+            if (k < top_k) {
+                const int e = idx[(size_t)t * top_k + k];
+                wg = gate_ptrs[e]; wu = up_ptrs[e]; wd = down_ptrs[e];
+                w = wt[(size_t)t * top_k + k];
+            } else {
+                if (!sh_gate || !sh_up || !sh_down) break;
+                wg = sh_gate; wu = sh_up; wd = sh_down;
+                w = sg_weight[t];
+            }
+            orc_matvec_f32(wg, ORC_Q4_K, xt, g, I, H);
+            orc_matvec_f32(wu, ORC_Q4_K, xt, u, I, H);
+            orc_swiglu(g, u, g, I);
+            orc_matvec_f32(wd, ORC_Q6_K, g, o, H, I);
+            for (int r = 0; r < H; r++) ot[r] += o[r] * w;
+        }
+    }
+    free(g);
+    free(u);
+    free(o);
+    return 0;
+}
+
+/* RMS normalisation with unit weight, as the pre-FFN norm
+ * (one_layer.cu:158-180, rmsnorm_inplace; layer_ops.cu:203-212) in fp64:
+ * y = x / sqrt(mean(x^2) + eps). */
+void orc_rmsnorm_f64(const double *x, double *y, int n, double eps)
+{
+    double ss = 0.0;
+    for (int i = 0; i < n; i++) ss += x[i] * x[i];
+    const double inv = 1.0 / sqrt(ss / (double)n + eps);
+    for (int i = 0; i < n; i++) y[i] = x[i] * inv;
+}

@@ -1,0 +1,142 @@
+"""GPU: Q4_K / Q6_K / Q8_0 GEMV parity.  Bar: relative L2 error <= 1e-3
+against an fp64-accumulated product of the exactly dequantised weights
+(oracle.matvec_f64)."""
+import numpy as np
+import pytest
+import torch
+
+import breadv2_b200 as bb
+from oracle import blocks as B
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def dev(a, cuda):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+SHAPES = [
+    (12, 512, 2048),   # config 1: one expert gate_proj
+    (14, 2048, 512),   # config 2: one expert down_proj
+    (12, 64, 256), (12, 130, 512), (12, 37, 1024), (12, 100, 4096),   # cols/256 = 1, 2 (ragged), 4, 16
+    (14, 96, 256), (14, 33, 1024), (14, 64, 2048), (14, 50, 4096),
+    (12, 16, 768), (14, 9, 1536),                                     # cols/256 = 3, 6: generic path
+    (8, 64, 2048), (8, 5, 96),                                        # Q8_0
+    (12, 1, 2048), (14, 1, 512),                                      # one row
+]
+
+
+@pytest.mark.parametrize("qt,rows,cols", SHAPES)
+def test_matvec_f32(cuda, orc, qt, rows, cols):
+    rng = np.random.default_rng(rows * 7 + cols + qt)
+    w = B.matrix(qt, rng, rows, cols)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = bb.matvec_f32(dev(w, cuda), dev(x, cuda), rows, cols, qt).cpu().numpy()
+    ref = orc.matvec_f64(w, qt, x, rows, cols)
+    assert orc.rel_l2(y, ref) < TOL
+
+
+@pytest.mark.parametrize("qt", [12, 14])
+@pytest.mark.parametrize("mode", ["subnormal", "zero_scale", "large", "mixed"])
+def test_matvec_weight_modes(cuda, orc, qt, mode):
+    rng = np.random.default_rng(31)
+    rows, cols = 256, 2048
+    w = B.matrix(qt, rng, rows, cols, mode)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = bb.matvec_f32(dev(w, cuda), dev(x, cuda), rows, cols, qt).cpu().numpy()
+    ref = orc.matvec_f64(w, qt, x, rows, cols)
+    if mode == "zero_scale" and qt == 12:
+        assert np.all(y == 0)
+    else:
+        assert orc.rel_l2(y, ref) < TOL
+
+
+@pytest.mark.parametrize("qt", [12, 14])
+def test_matvec_activation_edges(cuda, orc, qt):
+    rng = np.random.default_rng(3)
+    rows, cols = 128, 2048
+    w = B.matrix(qt, rng, rows, cols)
+    wd = dev(w, cuda)
+    x0 = np.zeros(cols, np.float32)
+    assert np.all(bb.matvec_f32(wd, dev(x0, cuda), rows, cols, qt).cpu().numpy() == 0)
+    x = rng.standard_normal(cols).astype(np.float32)
+    x[17] = 3e4          # one outlier: its 32-value group keeps ~16 bits around it
+    x[100:132] = 1e-30   # a group of tiny values
+    y = bb.matvec_f32(wd, dev(x, cuda), rows, cols, qt).cpu().numpy()
+    assert orc.rel_l2(y, orc.matvec_f64(w, qt, x, rows, cols)) < TOL
+    xn = x.copy()
+    xn[5] = np.nan
+    yn = bb.matvec_f32(wd, dev(xn, cuda), rows, cols, qt).cpu().numpy()
+    assert np.all(np.isnan(yn))
+
+
+@pytest.mark.parametrize("qt,rows,cols", [(12, 512, 2048), (14, 2048, 512), (12, 33, 512)])
+def test_matvec_unaligned_weights(cuda, orc, qt, rows, cols):
+    """Weights at a 2-byte offset take the alignment-agnostic path."""
+    rng = np.random.default_rng(11)
+    w = B.matrix(qt, rng, rows, cols)
+    buf = torch.zeros(w.size + 16, dtype=torch.uint8, device=cuda)
+    buf[2:2 + w.size] = dev(w, cuda)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = torch.empty(rows, dtype=torch.float32, device=cuda)
+    bb.check(bb.lib().bread_matvec_f32(bb._p(buf.data_ptr() + 2), bb._p(dev(x, cuda)), bb._p(y), rows, cols, qt,
+                                       bb._s(None)), "matvec")
+    assert orc.rel_l2(y.cpu().numpy(), orc.matvec_f64(w, qt, x, rows, cols)) < TOL
+
+
+@pytest.mark.parametrize("qt,rows,cols", [(12, 512, 2048), (14, 2048, 512), (12, 8, 256)])
+def test_matvec_f16_dropin(cuda, orc, qt, rows, cols):
+    """bread_matvec (kernels.cu:289): fp16 x, fp16 y."""
+    rng = np.random.default_rng(21)
+    w = B.matrix(qt, rng, rows, cols)
+    xh = rng.standard_normal(cols).astype(np.float16)
+    y = torch.empty(rows, dtype=torch.float16, device=cuda)
+    bb.matvec(dev(w, cuda), dev(xh, cuda), y, rows, cols, qt)
+    ref = orc.matvec_f64(w, qt, xh.astype(np.float32), rows, cols)
+    # fp16 output rounding alone is ~2.9e-4 relative (rms)
+    assert orc.rel_l2(y.float().cpu().numpy(), ref) < 2e-3
+
+
+def test_matvec_kat_selftest(cuda):
+    """The reference self-test shape (kernels.cu:451-579): 8 rows x 1 block, x = 1."""
+    x = torch.ones(256, dtype=torch.float16, device=cuda)
+    for blk, qt, exp in ((B.kat_q4k_block(), 12, 1792.0), (B.kat_q6k_block(), 14, 2048.0)):
+        y = torch.empty(8, dtype=torch.float16, device=cuda)
+        bb.matvec(dev(np.tile(blk, 8), cuda), x, y, 8, 256, qt)
+        assert torch.all(y.float() == exp)
+
+
+@pytest.mark.parametrize("T", [2, 5, 8, 16])
+@pytest.mark.parametrize("qt,rows,cols", [(12, 512, 2048), (14, 2048, 512)])
+def test_matvec_batch(cuda, orc, T, qt, rows, cols):
+    rng = np.random.default_rng(T)
+    w = B.matrix(qt, rng, rows, cols)
+    x = rng.standard_normal((T, cols)).astype(np.float32)
+    y = bb.matvec_f32(dev(w, cuda), dev(x, cuda), rows, cols, qt).cpu().numpy()
+    ref = orc.matvec_f64(w, qt, x, rows, cols)
+    for t in range(T):
+        assert orc.rel_l2(y[t], ref[t]) < TOL
+
+
+def test_lm_head_q6k_full_size(cuda, orc):
+    """Config 2's 248320 x 2048 Q6_K output head (417 MB): synthetic weights on
+    the device; 512 random rows checked against the oracle, plus linearity of
+    the whole product."""
+    rows, cols = 248320, 2048
+    nb = rows * cols // 256
+    w = bb.synth_blocks(nb, 14, 99, 1, device=cuda)
+    rng = np.random.default_rng(4)
+    x1 = rng.standard_normal(cols).astype(np.float32)
+    x2 = rng.standard_normal(cols).astype(np.float32)
+    y1 = bb.matvec_f32(w, dev(x1, cuda), rows, cols, 14)
+    y2 = bb.matvec_f32(w, dev(x2, cuda), rows, cols, 14)
+    y12 = bb.matvec_f32(w, dev(x1 + 2 * x2, cuda), rows, cols, 14)
+    torch.cuda.synchronize()
+    lin = (y12 - (y1 + 2 * y2)).norm() / y12.norm()
+    assert lin.item() < 2 * TOL
+    pick = np.sort(rng.choice(rows, 512, replace=False))
+    rb = 8 * 210
+    wr = w.view(rows, rb)[torch.from_numpy(pick).to(cuda)].cpu().numpy().reshape(-1)
+    ref = orc.matvec_f64(wr, 14, x1, 512, cols)
+    assert orc.rel_l2(y1.cpu().numpy()[pick], ref) < TOL
