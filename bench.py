@@ -53,7 +53,7 @@ def layer_bytes(groups: int, pairs: int, T: int) -> dict:
     k1 = E * H * 4 + H * 2 + T * H * 4 + T * H * 2 + T * (H // 32) * 4 + T * E * 4
     k2 = groups * 2 * GATE_B + T * H * 2 + pairs * I * 2
     k3 = groups * DOWN_B + pairs * I * 2 + 2 * T * H * 4
-    return {"route": k1, "gateup": k2, "down": k3}
+    return {"route": k1, "gateup": k2, "down": k3, "combine": 0}
 
 
 class ClockSampler:
@@ -340,12 +340,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     ms_step = ms / args.steps
     value = T / (ms_step * 1e-3)
     bytes_per_layer = [layer_bytes(int(g), int(p), T) for g, p in zip(groups, pairs)]
-    names = ["route", "gateup", "down"]
+    names = ["route", "gateup", "down", "combine"]
     tot_ms = {n: float(kms[:, j].sum()) for j, n in enumerate(names)}
     tot_b = {n: float(sum(b[n] for b in bytes_per_layer)) for n in names}
-    dom = max(names, key=lambda n: tot_ms[n])
+    dom = max(names[:3], key=lambda n: tot_ms[n])
     achieved = tot_b[dom] / (tot_ms[dom] * 1e-3) / 1e9
-    kernel_names = {"route": "moe_route_kernel", "gateup": "moe_gateup_kernel<8>", "down": "moe_down_kernel<2>"}
+    kernel_names = {"route": "moe_route_kernel", "gateup": "moe_gateup_kernel<8>", "down": "moe_down_kernel<2>",
+                    "combine": "ep_combine_kernel"}
     traffic = None
     tfile = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tfile):

@@ -155,6 +155,8 @@ class ExpertStack:
         self.cfg = StackConfig(n_layers, hidden, inter, n_experts, top_k, max_tokens, int(shared_expert), norm_eps,
                                seed, rank, world)
         h = ctypes.c_void_p(0)
+        self.handle = None
+        self._opened = []
         check(lib().bread_stack_create(ctypes.byref(h), ctypes.byref(self.cfg)), "bread_stack_create")
         self.handle = h
 
@@ -162,6 +164,36 @@ class ExpertStack:
         if self.handle:
             lib().bread_stack_destroy(self.handle)
             self.handle = None
+        for p in self._opened:
+            lib().bread_ipc_close_handle(ctypes.c_void_p(p))
+        self._opened = []
+
+    def mailbox(self):
+        ptr, n = ctypes.c_void_p(0), ctypes.c_size_t(0)
+        check(lib().bread_stack_mailbox(self.handle, ctypes.byref(ptr), ctypes.byref(n)), "bread_stack_mailbox")
+        return ptr.value or 0, n.value
+
+    def connect_peers(self, dist, group=None) -> None:
+        """Expert parallel set-up: exchange CUDA IPC handles of every rank's
+        mailbox over `dist` (torch.distributed, any backend) and map the peers'."""
+        rank, world = self.cfg.rank, self.cfg.world
+        ptr, _ = self.mailbox()
+        handle = ctypes.create_string_buffer(64)
+        check(lib().bread_ipc_get_handle(ctypes.c_void_p(ptr), handle), "bread_ipc_get_handle")
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle.raw), group=group)
+        peers = []
+        for r, hb in enumerate(handles):
+            if r == rank:
+                peers.append(ptr)
+                continue
+            p = ctypes.c_void_p(0)
+            buf = ctypes.create_string_buffer(bytes(hb), 64)
+            check(lib().bread_ipc_open_handle(buf, ctypes.byref(p)), "bread_ipc_open_handle")
+            self._opened.append(p.value)
+            peers.append(p.value)
+        arr = (ctypes.c_void_p * world)(*peers)
+        check(lib().bread_stack_set_peers(self.handle, arr, world), "bread_stack_set_peers")
 
     def __del__(self):
         try:
@@ -191,14 +223,14 @@ class ExpertStack:
         check(lib().bread_stack_step(self.handle, _p(h), h.shape[0], _s(stream)), "bread_stack_step")
 
     def profile_step(self, h, stream=None):
-        """One instrumented step; returns per-layer (route, gate/up, down) ms."""
+        """One instrumented step; returns per-layer (route, gate/up, down, combine) ms."""
         import numpy as np
 
         L = self.cfg.n_layers
-        out = np.zeros(3 * L, dtype=np.float32)
+        out = np.zeros(4 * L, dtype=np.float32)
         check(lib().bread_stack_profile_step(self.handle, _p(h), h.shape[0], _s(stream),
                                              out.ctypes.data_as(ctypes.c_void_p)), "bread_stack_profile_step")
-        return out.reshape(L, 3)
+        return out.reshape(L, 4)
 
     def routing_stats(self):
         """Per layer of the last step: (expert groups computed here, token-expert pairs)."""

@@ -40,6 +40,9 @@ SIGNATURES = {
     "bread_stack_layer": (_I, [_P, _I] + [ctypes.POINTER(_P)] * 8 + [ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "bread_stack_mailbox": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_SZ)]),
     "bread_stack_set_peers": (_I, [_P, ctypes.POINTER(_P), _I]),
+    "bread_ipc_get_handle": (_I, [_P, _P]),
+    "bread_ipc_open_handle": (_I, [_P, ctypes.POINTER(_P)]),
+    "bread_ipc_close_handle": (_I, [_P]),
     "bread_stack_step": (_I, [_P, _P, _I, _P]),
     "bread_stack_step_host": (_I, [_P, _P, _P, _I, _P]),
     "bread_stack_launches_per_step": (_I, [_P, _I]),

@@ -56,39 +56,42 @@ __device__ __forceinline__ float warp_sum(float v)
     return v;
 }
 
+// Runs in the last K1 CTA to finish (256 threads).  Latency matters here (it
+// sits between the router GEMV and the expert kernels), so every global input
+// is loaded in one round of independent loads and the routing stays in shared
+// memory for the grouping.
 __device__ void moe_finalize(const MoeArgs &a)
 {
     __shared__ int s_cnt[MOE_EMAX], s_run[MOE_EMAX], s_off[MOE_EMAX], s_gcnt[MOE_EMAX + 1];
     __shared__ float s_rinv[MOE_TMAX];
+    __shared__ int s_idx[MOE_TMAX * MOE_KMAX];
+    __shared__ float s_w[MOE_TMAX * MOE_KMAX], s_sgw[MOE_TMAX];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = a.T, H = a.H, E = a.E, K = a.top_k, HG = H / 32;
-
-    // (a) RMS factors from the per-group sums of squares K1 wrote
-    for (int t = warp; t < T; t += 8) {
-        float ss = 0.0f;
-        for (int g = lane; g < HG; g += 32) ss += __ldcg(a.ssq + t * HG + g);
-        ss = warp_sum(ss);
-        if (lane == 0) s_rinv[t] = a.norm_eps >= 0.0f ? rsqrtf(ss / (float)H + a.norm_eps) : 1.0f;
-    }
     for (int i = tid; i < MOE_EMAX; i += blockDim.x) {
         s_cnt[i] = 0;
         s_run[i] = 0;
     }
-    __syncthreads();
-    // (b) activation scales of the normalised input
-    if (a.norm_eps >= 0.0f)
-        for (int i = tid; i < T * HG; i += blockDim.x) a.xs[i] = __ldcg(a.xs + i) * s_rinv[i / HG];
 
-    // (c) softmax + top-k, one warp per token (layer_ops.cu:222-250)
+    // (a) per token (one warp each): RMS factor, softmax, top-k
+    //     (layer_ops.cu:222-250), renormalised weights, shared-gate sigmoid
     constexpr int PER = MOE_EMAX / 32;
     for (int t = warp; t < T; t += 8) {
-        const float r = s_rinv[t];
         float p[PER];
-        float m = -INFINITY;
 #pragma unroll
         for (int j = 0; j < PER; ++j) {
             const int e = lane + 32 * j;
-            p[j] = e < E ? __ldcg(a.logits + (size_t)t * E + e) * r : -INFINITY;
+            p[j] = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
+        }
+        float ss = 0.0f;
+        for (int g = lane; g < HG; g += 32) ss += __ldcg(a.ssq + t * HG + g);
+        const float score = __ldcg(a.score + t);
+        ss = warp_sum(ss);
+        const float r = a.norm_eps >= 0.0f ? rsqrtf(ss / (float)H + a.norm_eps) : 1.0f;
+        float m = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            p[j] *= r;
             m = fmaxf(m, p[j]);
         }
 #pragma unroll
@@ -96,8 +99,7 @@ __device__ void moe_finalize(const MoeArgs &a)
         float s = 0.0f;
 #pragma unroll
         for (int j = 0; j < PER; ++j) {
-            const int e = lane + 32 * j;
-            p[j] = e < E ? expf(p[j] - m) : 0.0f;
+            p[j] = (lane + 32 * j) < E ? expf(p[j] - m) : 0.0f;
             s += p[j];
         }
         s = warp_sum(s);
@@ -133,29 +135,35 @@ __device__ void moe_finalize(const MoeArgs &a)
         }
         if (lane < K) {
             const float w = wsum > 0.0f ? my_w / wsum : my_w;
+            s_idx[t * K + lane] = my_i;
+            s_w[t * K + lane] = w;
             a.ridx[t * K + lane] = my_i;
             a.rw[t * K + lane] = w;
             if (a.idx_out) a.idx_out[t * K + lane] = my_i;
             if (a.w_out) a.w_out[t * K + lane] = w;
         }
         if (lane == 0) {
-            const float sg = a.w_sg ? 1.0f / (1.0f + expf(-(__ldcg(a.score + t) * r))) : 0.5f;
+            const float sg = a.w_sg ? 1.0f / (1.0f + expf(-(score * r))) : 0.5f;
+            s_rinv[t] = r;
+            s_sgw[t] = sg;
             a.sgw[t] = sg;
             if (a.sg_out) a.sg_out[t] = sg;
         }
     }
     __syncthreads();
 
-    // (d) pairs per local expert
+    // (b) scales of the normalised activations; pairs per local expert
+    if (a.norm_eps >= 0.0f)
+        for (int i = tid; i < T * HG; i += blockDim.x) a.xs[i] = __ldcg(a.xs + i) * s_rinv[i / HG];
     const int P = T * K;
     for (int q = tid; q < P; q += blockDim.x) {
-        const int e = __ldcg(a.ridx + q);
+        const int e = s_idx[q];
         if (e >= a.lo && e < a.hi) atomicAdd(&s_cnt[e - a.lo], 1);
     }
     __syncthreads();
     if (warp != 0) return;
 
-    // (e) groups: shared expert first, then routed experts by ascending id
+    // (c) groups: shared expert first, then routed experts by ascending id
     const int NL = a.hi - a.lo;
     const int hs = a.shared_here ? 1 : 0;
     int gbase = hs, pbase = hs ? T : 0;
@@ -215,13 +223,13 @@ __device__ void moe_finalize(const MoeArgs &a)
             a.stats[1] = pbase;
         }
     }
-    // (f) place pairs, token-major inside each expert (deterministic)
+    // (d) place pairs, token-major inside each expert (deterministic)
     for (int q0 = 0; q0 < P; q0 += 32) {
         const int q = q0 + lane;
         int e = -1;
         bool loc = false;
         if (q < P) {
-            e = __ldcg(a.ridx + q);
+            e = s_idx[q];
             loc = e >= a.lo && e < a.hi;
         }
         const unsigned act = __ballot_sync(0xffffffffu, loc);
@@ -231,7 +239,7 @@ __device__ void moe_finalize(const MoeArgs &a)
             const int el = e - a.lo;
             const int pos = s_off[el] + s_run[el] + rank;
             a.p_token[pos] = q / K;
-            a.p_w[pos] = __ldcg(a.rw + q);
+            a.p_w[pos] = s_w[q];
             if (__ffs(peers) - 1 == lane) s_run[el] += __popc(peers);
         }
         __syncwarp();
@@ -239,7 +247,7 @@ __device__ void moe_finalize(const MoeArgs &a)
     if (hs)
         for (int t = lane; t < T; t += 32) {
             a.p_token[t] = t;
-            a.p_w[t] = __ldcg(a.sgw + t);
+            a.p_w[t] = s_sgw[t];
         }
     if (lane == 0) a.hdr[HDR_TICKET] = 0;  // re-armed for the next launch
 }
@@ -548,10 +556,78 @@ __global__ void __launch_bounds__(288) moe_down_kernel(MoeArgs a)
                 s += accs[(size_t)w * T * MOE_RT3 + i];
                 accs[(size_t)w * T * MOE_RT3 + i] = 0.0f;
             }
-            float *o = a.out + (size_t)t * a.H + (size_t)it * MOE_RT3 + r;
-            *o = *o + s;
+            const size_t oi = (size_t)t * a.H + (size_t)it * MOE_RT3 + r;
+            if (a.ep_world > 1) {
+                // partial of this rank -> slot [ep_slot][ep_rank] of every rank's mailbox (NVLink stores)
+                const size_t off = MoeMailbox::data_off(a.ep_slot, a.ep_rank, a.ep_world, a.ep_tmax, a.H) / 4 + oi;
+                for (int p = 0; p < a.ep_world; ++p) a.ep_mb[p][off] = s;
+            } else {
+                a.out[oi] = a.out[oi] + s;
+            }
         }
         named_sync(1, 256);
+    }
+    if (a.ep_world > 1) {
+        // one arrival per CTA at every rank, after all of this CTA's stores
+        __threadfence_system();
+        named_sync(1, 256);
+        if (tid == 0) {
+            const MoeMailbox L = MoeMailbox::make(a.ep_world, a.ep_tmax, a.H);
+            for (int p = 0; p < a.ep_world; ++p) {
+                unsigned *f = reinterpret_cast<unsigned *>(reinterpret_cast<uint8_t *>(a.ep_mb[p]) + L.flag_off) +
+                              a.ep_slot * 8 + a.ep_rank;
+                atomicAdd_system(f, 1u);
+            }
+        }
+    }
+}
+
+// Expert-parallel combine (one per layer, after K3 on every rank): wait,
+// bounded, until every rank's K3 CTAs have arrived in this rank's mailbox
+// slot, then h += sum over ranks (rank order, so every rank gets the same
+// bits); the last CTA re-arms the slot's counters.
+__global__ void __launch_bounds__(256) ep_combine_kernel(float *h, MoeArgs a, int n_signals)
+{
+    uint8_t *own = reinterpret_cast<uint8_t *>(a.ep_mb[a.ep_rank]);
+    const MoeMailbox L = MoeMailbox::make(a.ep_world, a.ep_tmax, a.H);
+    volatile unsigned *flags = reinterpret_cast<volatile unsigned *>(own + L.flag_off) + a.ep_slot * 8;
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        for (int r = 0; r < a.ep_world && ok; ++r) {
+            long long i = 0;
+            while (flags[r] < (unsigned)n_signals) {
+                if (++i > SPIN_LIMIT) {
+                    ok = 0;
+                    flag_error(DEVERR_TIMEOUT);
+                    break;
+                }
+                if (i > 64) __nanosleep(128);
+            }
+        }
+        __threadfence_system();
+        s_ok = ok;
+    }
+    __syncthreads();
+    if (s_ok) {
+        const float *mb = reinterpret_cast<const float *>(own);
+        const size_t n = (size_t)a.T * a.H;
+        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+            float v = h[i];
+            for (int r = 0; r < a.ep_world; ++r)
+                v += __ldcv(mb + MoeMailbox::data_off(a.ep_slot, r, a.ep_world, a.ep_tmax, a.H) / 4 + i);
+            h[i] = v;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned *ticket = reinterpret_cast<unsigned *>(own + L.ticket_off) + a.ep_slot;
+        __threadfence();
+        if (atomicAdd(ticket, 1u) == gridDim.x - 1) {
+            for (int r = 0; r < a.ep_world; ++r) flags[r] = 0;
+            *ticket = 0;
+            __threadfence_system();
+        }
     }
 }
 
@@ -606,16 +682,23 @@ int moe_launch_route(const MoeArgs &a, cudaStream_t s)
 }
 
 template <int NB>
+static int setup_gateup_nb()
+{
+    static bool done = false;
+    if (!done) {
+        BREAD_CUDA(cudaFuncSetAttribute(moe_gateup_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)K2Cfg<NB>::SMEM),
+                   "moe gate/up smem attribute");
+        done = true;
+    }
+    return BREAD_OK;
+}
+
+template <int NB>
 static int launch_gateup_nb(const MoeArgs &a, cudaStream_t s)
 {
-    using C = K2Cfg<NB>;
-    static bool attr = false;
-    if (!attr) {
-        BREAD_CUDA(cudaFuncSetAttribute(moe_gateup_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM),
-                   "moe gate/up smem attribute");
-        attr = true;
-    }
-    moe_gateup_kernel<NB><<<sm_count(), 288, C::SMEM, s>>>(a);
+    BREAD_TRY(setup_gateup_nb<NB>());
+    moe_gateup_kernel<NB><<<sm_count(), 288, K2Cfg<NB>::SMEM, s>>>(a);
     BREAD_CUDA(cudaGetLastError(), "moe gate/up launch");
     return BREAD_OK;
 }
@@ -632,25 +715,75 @@ int moe_launch_gateup(const MoeArgs &a, cudaStream_t s)
     }
 }
 
+// Grid of K3 for these shapes (also the number of arrivals each rank's
+// combine waits for).  The smem attribute and occupancy are set up once.
+template <int NB>
+static int down_grid_nb(const MoeArgs &a)
+{
+    using C = K3Cfg<NB>;
+    static int per_sm = 0;
+    if (!per_sm) {
+        if (cudaFuncSetAttribute(moe_down_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)C::smem(MOE_TMAX)) != cudaSuccess)
+            return -1;
+        int n = 1;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, moe_down_kernel<NB>, 288, C::smem(1)) != cudaSuccess)
+            return -1;
+        per_sm = n < 1 ? 1 : n;
+    }
+    const int items = a.H / MOE_RT3;
+    const int cap = sm_count() * (a.T <= 8 ? per_sm : 1);
+    return items < cap ? items : cap;
+}
+
 template <int NB>
 static int launch_down_nb(const MoeArgs &a, cudaStream_t s)
 {
     using C = K3Cfg<NB>;
-    static bool attr = false;
-    static int per_sm = 1;
-    if (!attr) {
-        BREAD_CUDA(cudaFuncSetAttribute(moe_down_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)C::smem(MOE_TMAX)),
-                   "moe down smem attribute");
-        BREAD_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_down_kernel<NB>, 288, C::smem(1)),
-                   "moe down occupancy");
-        if (per_sm < 1) per_sm = 1;
-        attr = true;
-    }
-    const int items = a.H / MOE_RT3;
-    const int cap = sm_count() * (a.T <= 8 ? per_sm : 1);
-    moe_down_kernel<NB><<<items < cap ? items : cap, 288, C::smem(a.T), s>>>(a);
+    const int grid = down_grid_nb<NB>(a);
+    if (grid < 1) return set_error(BREAD_ERR_CUDA, "moe down: kernel set-up failed");
+    moe_down_kernel<NB><<<grid, 288, C::smem(a.T), s>>>(a);
     BREAD_CUDA(cudaGetLastError(), "moe down launch");
+    return BREAD_OK;
+}
+
+int moe_down_grid(const MoeArgs &a)
+{
+    switch (a.I / 256) {
+    case 1: return down_grid_nb<1>(a);
+    case 2: return down_grid_nb<2>(a);
+    case 4: return down_grid_nb<4>(a);
+    default: return down_grid_nb<8>(a);
+    }
+}
+
+// One-time kernel attribute set-up for these shapes (before any graph capture).
+int moe_setup_kernels(int H, int I)
+{
+    int st = BREAD_OK;
+    switch (H / 256) {
+    case 1: st = setup_gateup_nb<1>(); break;
+    case 2: st = setup_gateup_nb<2>(); break;
+    case 4: st = setup_gateup_nb<4>(); break;
+    case 8: st = setup_gateup_nb<8>(); break;
+    case 16: st = setup_gateup_nb<16>(); break;
+    default: return set_error(BREAD_ERR_ARG, "moe: unsupported H=%d", H);
+    }
+    if (st) return st;
+    MoeArgs a{};
+    a.H = H;
+    a.I = I;
+    a.T = 1;
+    return moe_down_grid(a) > 0 ? BREAD_OK : set_error(BREAD_ERR_CUDA, "moe down: kernel set-up failed");
+}
+
+int moe_launch_combine(const MoeArgs &a, float *h, cudaStream_t s)
+{
+    const int n = a.T * a.H;
+    int grid = (n + 255) / 256;
+    if (grid > sm_count()) grid = sm_count();
+    ep_combine_kernel<<<grid, 256, 0, s>>>(h, a, moe_down_grid(a));
+    BREAD_CUDA(cudaGetLastError(), "ep combine launch");
     return BREAD_OK;
 }
 

@@ -83,6 +83,31 @@ struct MoeArgs {
     int *idx_out;
     float *w_out, *sg_out;
     int *stats;  // optional: [groups, pairs] computed here (written by K1)
+    // expert parallel (ep_world > 1): K3 stores its partial rows into every
+    // rank's mailbox instead of accumulating into `out`, then counts one
+    // arrival per CTA at every rank (MoeMailbox layout)
+    float *ep_mb[8];
+    int ep_world, ep_rank, ep_slot, ep_tmax;
+};
+
+// Mailbox of one rank (expert parallel): [MB_SLOTS][world][Tmax x H] fp32
+// partials, arrival counters [MB_SLOTS][8], combine tickets [MB_SLOTS].
+constexpr int MB_SLOTS = 3;
+struct MoeMailbox {
+    size_t flag_off, ticket_off, total;
+    __host__ __device__ static MoeMailbox make(int world, int Tmax, int H)
+    {
+        MoeMailbox m;
+        const size_t data = (size_t)MB_SLOTS * world * Tmax * H * 4;
+        m.flag_off = (data + 255) / 256 * 256;
+        m.ticket_off = m.flag_off + 256;
+        m.total = m.ticket_off + 256;
+        return m;
+    }
+    __host__ __device__ static size_t data_off(int slot, int src, int world, int Tmax, int H)
+    {
+        return ((size_t)slot * world + src) * Tmax * H * 4;
+    }
 };
 
 void moe_bind_workspace(MoeArgs &a, void *ws, const MoeWs &L);
@@ -91,6 +116,9 @@ int moe_check_shapes(int T, int H, int I, int E, int top_k, bool need_experts);
 int moe_launch_route(const MoeArgs &a, cudaStream_t s);
 int moe_launch_gateup(const MoeArgs &a, cudaStream_t s);
 int moe_launch_down(const MoeArgs &a, cudaStream_t s);
+int moe_down_grid(const MoeArgs &a);
+int moe_launch_combine(const MoeArgs &a, float *h, cudaStream_t s);
+int moe_setup_kernels(int H, int I);
 int moe_route_grid(const MoeArgs &a);
 
 }  // namespace bread

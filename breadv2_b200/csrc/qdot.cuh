@@ -88,10 +88,10 @@ __device__ __forceinline__ float elem_exact(const uint8_t *blk, int e)
 __device__ __forceinline__ int quant32(float v, float *scale, int lane)
 {
     float a = fabsf(v);
+    // fmaxf drops NaN, so non-finite values are detected separately
+    const bool finite = !__any_sync(0xffffffffu, !(a <= 3.402823466e38f));
 #pragma unroll
     for (int o = 16; o; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    const bool finite = a <= 3.402823466e38f;  // false for inf and NaN
-    a = __shfl_sync(0xffffffffu, finite ? a : __int_as_float(0x7fc00000), 0);
     int q = 0;
     if (a > 0.0f && finite) q = __float2int_rn((v / a) * 32767.0f);  // |v/a| <= 1, also for subnormal a
     if (lane == 0) *scale = finite ? a * (1.0f / 32767.0f) : __int_as_float(0x7fc00000);

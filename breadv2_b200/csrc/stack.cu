@@ -15,6 +15,8 @@
 // of every layer plus the shared expert of layers l with l % world == r; the
 // router (2 MB per layer) is replicated, so all ranks route identically and no
 // dispatch exchange is needed.
+#include <string.h>
+
 #include <map>
 #include <utility>
 #include <vector>
@@ -39,28 +41,6 @@ struct LayerW {
     const uint8_t **tab;                 // device: gate[E], up[E], down[E] pointer tables
 };
 
-// Mailbox of one rank: [2 parities][world][T_max x H] fp32 partials, then
-// flags [2][world] (arrival counts from each rank) and a local ticket.
-struct Mailbox {
-    size_t data_bytes, flag_off, ticket_off, total;
-    __host__ __device__ static Mailbox make(int world, int Tmax, int H)
-    {
-        Mailbox m;
-        m.data_bytes = (size_t)2 * world * Tmax * H * 4;
-        m.flag_off = (m.data_bytes + 255) / 256 * 256;
-        m.ticket_off = m.flag_off + 256;
-        m.total = m.ticket_off + 256;
-        return m;
-    }
-};
-
-struct EpArgs {
-    float *peer_mb[EP_MAXW];  // mailbox base of every rank (own included)
-    int rank, world, Tmax, H, T;
-    int parity;
-    int n_signals;            // K3 CTAs per rank (arrivals expected per rank)
-};
-
 }  // namespace bread
 
 struct bread_stack {
@@ -75,8 +55,9 @@ struct bread_stack {
     float *h_dev = nullptr;  // staging buffer of bread_stack_step_host
     // expert parallel
     uint8_t *mailbox = nullptr;
-    bread::Mailbox mbl;
+    bread::MoeMailbox mbl;
     bool peers_set = false;
+    cudaStream_t cap = nullptr;  // private stream graphs are captured on
     float *peer_mb[bread::EP_MAXW] = {};
     std::map<std::pair<int, float *>, cudaGraphExec_t> graphs;
     int *stats_dev = nullptr;  // [n_layers][2]: groups, pairs of the last step
@@ -84,60 +65,6 @@ struct bread_stack {
     std::vector<cudaEvent_t> ev;
     std::map<std::pair<int, float *>, cudaGraphExec_t> prof_graphs;
 };
-
-namespace bread {
-
-// ---- expert-parallel combine ------------------------------------------------
-// K3 (EP mode) ends by calling ep_publish: store the CTA's partial rows into
-// every rank's mailbox, then count one arrival per CTA at every rank.
-__global__ void ep_combine_kernel(float *h, EpArgs ep)
-{
-    // every CTA waits until all ranks' K3 CTAs have arrived
-    uint8_t *own = reinterpret_cast<uint8_t *>(ep.peer_mb[ep.rank]);
-    const Mailbox L = Mailbox::make(ep.world, ep.Tmax, ep.H);
-    volatile unsigned *flags = reinterpret_cast<volatile unsigned *>(own + L.flag_off) + ep.parity * EP_MAXW;
-    __shared__ int s_ok;
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        for (int r = 0; r < ep.world && ok; ++r) {
-            long long i = 0;
-            while (flags[r] < (unsigned)ep.n_signals) {
-                if (++i > SPIN_LIMIT) {
-                    ok = 0;
-                    flag_error(DEVERR_TIMEOUT);
-                    break;
-                }
-                if (i > 64) __nanosleep(128);
-            }
-        }
-        __threadfence_system();
-        s_ok = ok;
-    }
-    __syncthreads();
-    if (s_ok) {
-        const float *mb = reinterpret_cast<const float *>(own);
-        const size_t slot = (size_t)ep.Tmax * ep.H;
-        const size_t n = (size_t)ep.T * ep.H;
-        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-            float s = h[i];
-            for (int r = 0; r < ep.world; ++r) s += __ldcv(mb + ((size_t)ep.parity * ep.world + r) * slot + i);
-            h[i] = s;
-        }
-    }
-    // the last CTA out re-arms the flags of this parity
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned *ticket = reinterpret_cast<unsigned *>(own + L.ticket_off) + ep.parity;
-        __threadfence();
-        if (atomicAdd(ticket, 1u) == gridDim.x - 1) {
-            for (int r = 0; r < ep.world; ++r) flags[r] = 0;
-            *ticket = 0;
-            __threadfence_system();
-        }
-    }
-}
-
-}  // namespace bread
 
 using namespace bread;
 
@@ -156,6 +83,7 @@ extern "C" int bread_stack_destroy(bread_stack_t *st)
     for (auto &kv : st->graphs) cudaGraphExecDestroy(kv.second);
     for (auto &kv : st->prof_graphs) cudaGraphExecDestroy(kv.second);
     for (cudaEvent_t e : st->ev) cudaEventDestroy(e);
+    if (st->cap) cudaStreamDestroy(st->cap);
     for (void *p : st->allocs) cudaFree(p);
     delete st;
     return BREAD_OK;
@@ -244,8 +172,11 @@ extern "C" int bread_stack_create(bread_stack_t **out, const bread_stack_config_
         if (!rc) rc = stack_alloc(st, &p, (size_t)c.n_layers * 2 * sizeof(int), "stack: stats");
         st->stats_dev = (int *)p;
     }
+    if (!rc && cudaStreamCreateWithFlags(&st->cap, cudaStreamNonBlocking) != cudaSuccess)
+        rc = set_error(BREAD_ERR_CUDA, "stack: capture stream");
+    if (!rc) rc = moe_setup_kernels(H, I);
     if (!rc && c.world > 1) {
-        st->mbl = Mailbox::make(c.world, c.max_tokens, H);
+        st->mbl = MoeMailbox::make(c.world, c.max_tokens, H);
         void *p = nullptr;
         rc = stack_alloc(st, &p, st->mbl.total, "stack: mailbox");
         st->mailbox = (uint8_t *)p;
@@ -301,6 +232,33 @@ extern "C" int bread_stack_set_peers(bread_stack_t *st, void *const *peer_mailbo
     st->peers_set = true;
     for (auto &kv : st->graphs) cudaGraphExecDestroy(kv.second);
     st->graphs.clear();
+    for (auto &kv : st->prof_graphs) cudaGraphExecDestroy(kv.second);
+    st->prof_graphs.clear();
+    return BREAD_OK;
+}
+
+extern "C" int bread_ipc_get_handle(const void *dev_ptr, void *handle_out)
+{
+    if (!dev_ptr || !handle_out) return set_error(BREAD_ERR_ARG, "ipc_get_handle: NULL argument");
+    cudaIpcMemHandle_t h;
+    BREAD_CUDA(cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr)), "cudaIpcGetMemHandle");
+    memcpy(handle_out, &h, sizeof h);
+    return BREAD_OK;
+}
+
+extern "C" int bread_ipc_open_handle(const void *handle, void **dev_ptr)
+{
+    if (!handle || !dev_ptr) return set_error(BREAD_ERR_ARG, "ipc_open_handle: NULL argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    BREAD_CUDA(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    return BREAD_OK;
+}
+
+extern "C" int bread_ipc_close_handle(void *dev_ptr)
+{
+    if (!dev_ptr) return set_error(BREAD_ERR_ARG, "ipc_close_handle: NULL argument");
+    BREAD_CUDA(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle");
     return BREAD_OK;
 }
 
@@ -311,7 +269,13 @@ extern "C" int bread_stack_launches_per_step(const bread_stack_t *st, int T)
     return st->cfg.n_layers * (st->cfg.world > 1 ? 4 : 3);
 }
 
-// ev: NULL, or 4 events per layer recorded before K1, K2, K3 and after K3.
+// Mailbox slot of layer l: consecutive layers (also the last and the first
+// of the next step) always use different slots, which is what makes a slot
+// safe to overwrite (see ep_combine_kernel).
+static int mailbox_slot(int l, int L) { return (L & 1) && l == L - 1 ? 2 : (l & 1); }
+
+// ev: NULL, or 5 events per layer recorded before K1, K2, K3, the combine,
+// and at the end of the layer.
 static int stack_enqueue(bread_stack_t *st, float *h, int T, cudaStream_t s, const cudaEvent_t *ev = nullptr)
 {
     const bread_stack_config_t &c = st->cfg;
@@ -338,24 +302,35 @@ static int stack_enqueue(bread_stack_t *st, float *h, int T, cudaStream_t s, con
         a.x = h;
         a.out = h;
         a.stats = st->stats_dev + 2 * l;
+        if (c.world > 1) {
+            a.ep_world = c.world;
+            a.ep_rank = c.rank;
+            a.ep_slot = mailbox_slot(l, c.n_layers);
+            a.ep_tmax = c.max_tokens;
+            for (int r = 0; r < c.world; ++r) a.ep_mb[r] = st->peer_mb[r];
+        }
         moe_bind_workspace(a, st->ws, st->wsl);
-        if (ev) BREAD_CUDA(cudaEventRecord(ev[4 * l + 0], s), "stack: event");
+        if (ev) BREAD_CUDA(cudaEventRecordWithFlags(ev[5 * l + 0], s, cudaEventRecordExternal), "stack: event");
         BREAD_TRY(moe_launch_route(a, s));
-        if (ev) BREAD_CUDA(cudaEventRecord(ev[4 * l + 1], s), "stack: event");
+        if (ev) BREAD_CUDA(cudaEventRecordWithFlags(ev[5 * l + 1], s, cudaEventRecordExternal), "stack: event");
         BREAD_TRY(moe_launch_gateup(a, s));
-        if (ev) BREAD_CUDA(cudaEventRecord(ev[4 * l + 2], s), "stack: event");
+        if (ev) BREAD_CUDA(cudaEventRecordWithFlags(ev[5 * l + 2], s, cudaEventRecordExternal), "stack: event");
         BREAD_TRY(moe_launch_down(a, s));
-        if (ev) BREAD_CUDA(cudaEventRecord(ev[4 * l + 3], s), "stack: event");
+        if (ev) BREAD_CUDA(cudaEventRecordWithFlags(ev[5 * l + 3], s, cudaEventRecordExternal), "stack: event");
+        if (c.world > 1) BREAD_TRY(moe_launch_combine(a, h, s));
+        if (ev) BREAD_CUDA(cudaEventRecordWithFlags(ev[5 * l + 4], s, cudaEventRecordExternal), "stack: event");
     }
     return BREAD_OK;
 }
 
-static int capture(bread_stack_t *st, float *h, int T, cudaStream_t stream, const cudaEvent_t *ev, cudaGraphExec_t *out)
+// Captures one step into a graph on the stack's private stream (capture is
+// not allowed on the legacy default stream a caller may use).
+static int capture(bread_stack_t *st, float *h, int T, const cudaEvent_t *ev, cudaGraphExec_t *out)
 {
     cudaGraph_t g = nullptr;
-    BREAD_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "stack: begin capture");
-    const int rc = stack_enqueue(st, h, T, stream, ev);
-    const cudaError_t ce = cudaStreamEndCapture(stream, &g);
+    BREAD_CUDA(cudaStreamBeginCapture(st->cap, cudaStreamCaptureModeThreadLocal), "stack: begin capture");
+    const int rc = stack_enqueue(st, h, T, st->cap, ev);
+    const cudaError_t ce = cudaStreamEndCapture(st->cap, &g);
     if (rc != BREAD_OK) {
         if (g) cudaGraphDestroy(g);
         return rc;
@@ -367,16 +342,23 @@ static int capture(bread_stack_t *st, float *h, int T, cudaStream_t stream, cons
     return BREAD_OK;
 }
 
+static int ready(const bread_stack_t *st, const float *h, int T)
+{
+    if (!st || !h) return set_error(BREAD_ERR_ARG, "stack: NULL argument");
+    if (T < 1 || T > st->cfg.max_tokens) return set_error(BREAD_ERR_ARG, "stack: T=%d outside 1..%d", T, st->cfg.max_tokens);
+    if (st->cfg.world > 1 && !st->peers_set)
+        return set_error(BREAD_ERR_STATE, "stack: expert-parallel stack needs bread_stack_set_peers first");
+    return BREAD_OK;
+}
+
 extern "C" int bread_stack_step(bread_stack_t *st, float *h, int T, cudaStream_t stream)
 {
-    if (!st || !h) return set_error(BREAD_ERR_ARG, "stack_step: NULL argument");
-    if (T < 1 || T > st->cfg.max_tokens) return set_error(BREAD_ERR_ARG, "stack_step: T=%d outside 1..%d", T, st->cfg.max_tokens);
-    if (st->cfg.world > 1) return set_error(BREAD_ERR_STATE, "stack_step: expert-parallel combine not available in this build");
+    BREAD_TRY(ready(st, h, T));
     const auto key = std::make_pair(T, h);
     auto it = st->graphs.find(key);
     if (it == st->graphs.end()) {
         cudaGraphExec_t ge = nullptr;
-        BREAD_TRY(capture(st, h, T, stream, nullptr, &ge));
+        BREAD_TRY(capture(st, h, T, nullptr, &ge));
         it = st->graphs.emplace(key, ge).first;
     }
     BREAD_CUDA(cudaGraphLaunch(it->second, stream), "stack: graph launch");
@@ -385,26 +367,25 @@ extern "C" int bread_stack_step(bread_stack_t *st, float *h, int T, cudaStream_t
 
 extern "C" int bread_stack_profile_step(bread_stack_t *st, float *h, int T, cudaStream_t stream, float *kernel_ms)
 {
-    if (!st || !h || !kernel_ms) return set_error(BREAD_ERR_ARG, "stack_profile_step: NULL argument");
-    if (T < 1 || T > st->cfg.max_tokens) return set_error(BREAD_ERR_ARG, "stack_profile_step: T=%d", T);
-    if (st->cfg.world > 1) return set_error(BREAD_ERR_STATE, "stack_profile_step: expert-parallel combine not available in this build");
+    BREAD_TRY(ready(st, h, T));
+    if (!kernel_ms) return set_error(BREAD_ERR_ARG, "stack_profile_step: NULL kernel_ms");
     const int L = st->cfg.n_layers;
     if (st->ev.empty()) {
-        st->ev.resize((size_t)4 * L);
+        st->ev.resize((size_t)5 * L);
         for (auto &e : st->ev) BREAD_CUDA(cudaEventCreate(&e), "stack: create event");
     }
     const auto key = std::make_pair(T, h);
     auto it = st->prof_graphs.find(key);
     if (it == st->prof_graphs.end()) {
         cudaGraphExec_t ge = nullptr;
-        BREAD_TRY(capture(st, h, T, stream, st->ev.data(), &ge));
+        BREAD_TRY(capture(st, h, T, st->ev.data(), &ge));
         it = st->prof_graphs.emplace(key, ge).first;
     }
     BREAD_CUDA(cudaGraphLaunch(it->second, stream), "stack: graph launch");
     BREAD_CUDA(cudaStreamSynchronize(stream), "stack: profile sync");
     for (int l = 0; l < L; ++l)
-        for (int k = 0; k < 3; ++k)
-            BREAD_CUDA(cudaEventElapsedTime(kernel_ms + 3 * l + k, st->ev[4 * l + k], st->ev[4 * l + k + 1]),
+        for (int k = 0; k < 4; ++k)
+            BREAD_CUDA(cudaEventElapsedTime(kernel_ms + 4 * l + k, st->ev[5 * l + k], st->ev[5 * l + k + 1]),
                        "stack: elapsed time");
     return BREAD_OK;
 }

@@ -177,6 +177,12 @@ int bread_stack_layer(const bread_stack_t *st, int layer, const void **gate_base
  * = own mailbox) to bread_stack_set_peers. */
 int bread_stack_mailbox(bread_stack_t *st, void **ptr, size_t *bytes);
 int bread_stack_set_peers(bread_stack_t *st, void *const *peer_mailboxes, int world);
+/* CUDA IPC of a mailbox between the ranks' processes: 64-byte handle of a
+ * device allocation; open a peer's handle (peer access enabled lazily); close
+ * an opened mapping after bread_stack_destroy. */
+int bread_ipc_get_handle(const void *dev_ptr, void *handle_out);
+int bread_ipc_open_handle(const void *handle, void **dev_ptr);
+int bread_ipc_close_handle(void *dev_ptr);
 /* One decode step of T tokens through all layers.  h: device fp32 [T x H],
  * updated in place (h <- h + moe_l(norm(h)) for each layer l).  The first
  * call for a given T captures a CUDA graph; later calls replay it. */
@@ -188,8 +194,8 @@ int bread_stack_step_host(bread_stack_t *st, const float *h_in, float *h_out, in
 int bread_stack_launches_per_step(const bread_stack_t *st, int T);
 /* One step like bread_stack_step, from a second graph that records CUDA
  * events around every kernel; synchronises `stream` and writes the duration
- * in ms of K1 (route), K2 (gate/up), K3 (down + combine) of every layer to
- * kernel_ms[3*layer + k]. */
+ * in ms of the router, gate/up, down and expert-parallel combine kernels
+ * (0 with world = 1) of every layer to kernel_ms[4*layer + k], k = 0..3. */
 int bread_stack_profile_step(bread_stack_t *st, float *h, int T, cudaStream_t stream, float *kernel_ms);
 /* Per layer of the last step: expert groups computed here (distinct routed
  * experts + the shared expert) and (token, expert) pairs.  Synchronous. */

@@ -1,0 +1,28 @@
+"""GPU, >= 2 devices: the expert-parallel stack (experts split over ranks,
+partials combined through NVLink mailboxes) against the single-GPU stack."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2])
+def test_ep_stack_matches_single_gpu(world):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", "--master-port=29531",
+           os.path.join(HERE, "_ep_worker.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("{")][-1]
+    res = json.loads(line)
+    assert res["device_error"] == 0
+    assert res["ranks_bitwise_equal"] and res["replays_equal"]
+    assert res["rel_vs_single_gpu"] < 1e-5

@@ -73,7 +73,7 @@ def test_stack_config_size_two_layers(cuda, orc):
     """Full layer shapes (H=2048, I=512, 256 experts, top-8 + shared), 2 layers, T=1."""
     cfg = dict(hidden=2048, inter=512, n_experts=256, top_k=8, seed=3, eps=1e-6)
     st = bb.ExpertStack(n_layers=2, max_tokens=2, seed=3)
-    h0 = bb.synth_normal(2048, 1.0, 3, 42, device=cuda).view(1, 2048)
+    h0 = bb.synth_normal(2048, 1.0, 3, 43, device=cuda).view(1, 2048)
     h = h0.clone()
     st.step(h)
     torch.cuda.synchronize()
