@@ -34,6 +34,7 @@ SIGNATURES = {
     "bread_moe_route": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
     "bread_moe_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "bread_moe_ffn": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
+    "bread_moe_ffn_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
     "bread_stack_create": (_I, [ctypes.POINTER(_P), _P]),
     "bread_stack_destroy": (_I, [_P]),
     "bread_stack_device_bytes": (_SZ, [_P]),

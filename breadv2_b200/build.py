@@ -25,7 +25,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC", "-Xcompiler", "-O2",
          "--expt-relaxed-constexpr", f"-I{INCLUDE}", "-Wno-deprecated-gpu-targets"]
 
-SOURCES = ["errors.cu", "gemv.cu", "glue.cu", "moe.cu", "stack.cu", "synth.cu"]
+SOURCES = ["errors.cu", "gemv.cu", "glue.cu", "moe.cu", "noalloc.cu", "stack.cu", "synth.cu"]
 HEADERS = ["common.cuh", "ptx.cuh", "qdot.cuh", "moe.cuh"]
 
 

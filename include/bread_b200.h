@@ -139,6 +139,23 @@ int bread_moe_ffn(const void *const *gate_ptrs, const void *const *up_ptrs, cons
                   const float *x, float *out, int T, int H, int I, int E, int top_k, int *idx_out, float *w_out,
                   float *sg_out, void *workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* bread_moe_ffn for callers that cannot allocate device memory.  No
+ * counterpart in the reference.  Some engines give all free HBM to their
+ * resident weights and caches up front, so cudaMalloc has nothing left, and
+ * some host loops must not call cudaMalloc on the decode path because it can
+ * synchronise the device.  Same arguments and results as bread_moe_ffn minus
+ * the workspace: the scratch is a fixed 256 KiB device array inside the
+ * library (present on every GPU that loads it, until exit), enough for e.g.
+ * T <= 8 at H = 2048, I = 512, E = 256, top_k = 8; larger shapes return
+ * BREAD_ERR_WORKSPACE.  Allocates nothing.  The first call on each device looks
+ * up the array's device address (cudaGetSymbolAddress), so make it before any
+ * stream capture.  All calls on a device share the array: calls that overlap
+ * on the GPU race and must be ordered by the caller. */
+int bread_moe_ffn_noalloc(const void *const *gate_ptrs, const void *const *up_ptrs, const void *const *down_ptrs,
+                          const float *W_r, const void *w_sg, const void *sh_gate, const void *sh_up,
+                          const void *sh_down, const float *x, float *out, int T, int H, int I, int E, int top_k,
+                          int *idx_out, float *w_out, float *sg_out, cudaStream_t stream);
+
 /* ---------------------------------------------------------------------- */
 /* Expert stack executor (the decode loop's MoE part, main.cu:683-687)     */
 /* ---------------------------------------------------------------------- */
