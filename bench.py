@@ -253,7 +253,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     T = args.batch
-    st = bb.ExpertStack(n_layers=LAYERS, hidden=H, inter=I, n_experts=E, top_k=K_TOP, max_tokens=T,
+    st = bb.ExpertStack(n_layers=args.layers, hidden=H, inter=I, n_experts=E, top_k=K_TOP, max_tokens=T,
                         shared_expert=True, norm_eps=1e-6, seed=args.seed, rank=rank, world=world)
     if world > 1:
         st.connect_peers(dist)
@@ -397,6 +397,8 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1, help="tokens per decode step (T)")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layers in the stack (profiling of small cases only; the benchmark is 40)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true",

@@ -10,14 +10,29 @@ constexpr int MOE_EMAX = 512;    // routed experts
 constexpr int MOE_KMAX = 16;     // top-k
 constexpr int MOE_HMAX = 4096;   // hidden size
 constexpr int MOE_IMAX = 2048;   // expert intermediate size
-constexpr int MOE_TC = 8;        // tokens per gate/up work item
+constexpr int MOE_TC = 8;        // (token, expert) pairs per chunk
 constexpr int MOE_ROWTILE = 32;  // gate/up rows per work item (one activation group)
 constexpr int MOE_RT3 = 16;      // down rows (= output rows) per work item
+constexpr int K1_TG = 4;         // tokens per router CTA
+
+// One chunk of up to MOE_TC pairs of one expert group, with everything the
+// expert kernels need to start their bulk copies: resolved weight pointers,
+// the pairs' first index (pairs of a group are contiguous), their tokens and
+// routing weights.  Written by the router's finalize step; 16-byte aligned so
+// that it can itself be bulk-copied into shared memory.
+struct __align__(16) MoeChunk {
+    const uint8_t *gate, *up, *down;
+    int p0, np, group, pad;
+    uint8_t tok[MOE_TC];
+    float w[MOE_TC];
+    uint8_t pad2[8];
+};
+static_assert(sizeof(MoeChunk) == 96, "MoeChunk layout");
 
 // Byte offsets of the pieces of a MoE workspace (all 256-byte aligned).
 struct MoeWs {
-    size_t logits, ssq, score, hdr, ridx, rw, sgw, xq, xs, g_expert, g_off, g_cnt, g_cpre, p_token, p_w, aq, as, total;
-    int GM, PM;
+    size_t hdr, logits, ssq, score, ridx, rw, sgw, xq, xs, p_token, p_w, chunks, aq, as, total;
+    int GM, PM, CM;
     static MoeWs make(int T, int H, int I, int E, int k)
     {
         MoeWs w;
@@ -29,6 +44,7 @@ struct MoeWs {
         };
         w.GM = (E < T * k ? E : T * k) + 1;
         w.PM = T * (k + 1);
+        w.CM = w.GM + (w.PM + MOE_TC - 1) / MOE_TC;
         w.hdr = take(64);
         w.logits = take((size_t)T * E * 4);
         w.ssq = take((size_t)T * (H / 32) * 4);
@@ -38,12 +54,9 @@ struct MoeWs {
         w.sgw = take((size_t)T * 4);
         w.xq = take((size_t)T * H * 2);
         w.xs = take((size_t)T * (H / 32) * 4);
-        w.g_expert = take((size_t)w.GM * 4);
-        w.g_off = take((size_t)(w.GM + 1) * 4);
-        w.g_cnt = take((size_t)w.GM * 4);
-        w.g_cpre = take((size_t)(w.GM + 1) * 4);
         w.p_token = take((size_t)w.PM * 4);
         w.p_w = take((size_t)w.PM * 4);
+        w.chunks = take((size_t)w.CM * sizeof(MoeChunk));
         w.aq = take((size_t)w.PM * (I > 0 ? I : 1) * 2);
         w.as = take((size_t)w.PM * (I > 0 ? I / 32 : 1) * 4);
         w.total = o;
@@ -52,9 +65,9 @@ struct MoeWs {
 };
 
 // Header words at MoeWs::hdr.
-enum { HDR_TICKET = 0, HDR_NGROUPS = 1, HDR_NCHUNKS = 2 };
+enum { HDR_TICKET = 0, HDR_NGROUPS = 1, HDR_NCHUNKS = 2, HDR_NPAIRS = 3 };
 
-// Everything the three MoE kernels read or write (passed by value).
+// Everything the MoE kernels read or write (passed by value).
 struct MoeArgs {
     const uint8_t *const *gate;  // device tables [E] (routed experts)
     const uint8_t *const *up;
@@ -75,17 +88,18 @@ struct MoeArgs {
     float *rw, *sgw;
     int16_t *xq;
     float *xs;
-    int *g_expert, *g_off, *g_cnt, *g_cpre, *p_token;
+    int *p_token;
     float *p_w;
+    MoeChunk *chunks;
     int16_t *aq;
     float *as;
     // optional routing copies
     int *idx_out;
     float *w_out, *sg_out;
-    int *stats;  // optional: [groups, pairs] computed here (written by K1)
-    // expert parallel (ep_world > 1): K3 stores its partial rows into every
-    // rank's mailbox instead of accumulating into `out`, then counts one
-    // arrival per CTA at every rank (MoeMailbox layout)
+    int *stats;  // optional: [groups, pairs] computed here (written by the router)
+    // expert parallel (ep_world > 1): the down kernel stores its partial rows
+    // into every rank's mailbox instead of accumulating into `out`, then
+    // counts one arrival per CTA at every rank (MoeMailbox layout)
     float *ep_mb[8];
     int ep_world, ep_rank, ep_slot, ep_tmax;
 };
@@ -112,13 +126,13 @@ struct MoeMailbox {
 
 void moe_bind_workspace(MoeArgs &a, void *ws, const MoeWs &L);
 int moe_check_shapes(int T, int H, int I, int E, int top_k, bool need_experts);
-// K1 (router + finalize), K2 (gate/up + SiLU*mul), K3 (down + combine).
+// Router + finalize, gate/up + SiLU*mul, down + combine, expert-parallel
+// combine.  All are launched with programmatic dependent launch allowed.
 int moe_launch_route(const MoeArgs &a, cudaStream_t s);
 int moe_launch_gateup(const MoeArgs &a, cudaStream_t s);
 int moe_launch_down(const MoeArgs &a, cudaStream_t s);
 int moe_down_grid(const MoeArgs &a);
 int moe_launch_combine(const MoeArgs &a, float *h, cudaStream_t s);
 int moe_setup_kernels(int H, int I);
-int moe_route_grid(const MoeArgs &a);
 
 }  // namespace bread
