@@ -49,11 +49,32 @@ def peaks():
 
 
 def layer_bytes(groups: int, pairs: int, T: int) -> dict:
-    """Algorithmic bytes of one layer's three kernels (each weight byte once)."""
+    """Algorithmic bytes of one layer's three phases (each weight byte once)."""
     k1 = E * H * 4 + H * 2 + T * H * 4 + T * H * 2 + T * (H // 32) * 4 + T * E * 4
     k2 = groups * 2 * GATE_B + T * H * 2 + pairs * I * 2
     k3 = groups * DOWN_B + pairs * I * 2 + 2 * T * H * 4
     return {"route": k1, "gateup": k2, "down": k3, "combine": 0}
+
+
+STAMP_POINTS = ["start", "logits", "router_barrier", "routed", "x_landed", "gateup_done", "gateup_barrier",
+                "down_landed", "down_done", "end", "p_routed", "p_gateup_issued", "p_down_issued", "p_router_issued",
+                "p_gateup_barrier", "p_down_all_issued"]
+
+
+def layer_timeline(stamps) -> dict:
+    """Timeline of a layer over all CTAs from the phase stamps [layers, ctas,
+    16] (ns): median and max over CTAs of each phase point, in us from the
+    earliest start of the layer, averaged over layers.  A point a CTA never
+    reaches (no work of that kind) stays 0 and is left out of the median."""
+    import numpy as np
+
+    s = stamps.astype(np.float64)
+    st0 = s[:, :, 0].min(axis=1)[:, None, None]
+    rel = np.where(s > 0, (s - st0) * 1e-3, np.nan)
+    med = np.nanmean(np.nanmedian(rel, axis=1), axis=0)
+    mx = np.nanmean(np.nanmax(rel, axis=1), axis=0)
+    return {"points": STAMP_POINTS, "median_us": [round(float(v), 2) for v in med],
+            "max_us": [round(float(v), 2) for v in mx]}
 
 
 class ClockSampler:
@@ -321,9 +342,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     ms_e2e = e2.elapsed_time(e3)
     clk = clocks.stop()
 
-    # per-kernel durations (instrumented replay of the same step) and routing stats
+    # phase durations (a profiled launch of the same step: every CTA records
+    # %globaltimer at its phase points) and routing stats
     h.copy_(inputs[0])
     kms = st.profile_step(h)
+    stamps = st.profile_stamps()
     groups, pairs = st.routing_stats()
     assert bb.device_error() == 0, "device-side wait timed out"
 
@@ -342,20 +365,19 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     bytes_per_layer = [layer_bytes(int(g), int(p), T) for g, p in zip(groups, pairs)]
     names = ["route", "gateup", "down", "combine"]
     tot_ms = {n: float(kms[:, j].sum()) for j, n in enumerate(names)}
-    tot_b = {n: float(sum(b[n] for b in bytes_per_layer)) for n in names}
-    dom = max(names[:3], key=lambda n: tot_ms[n])
-    achieved = tot_b[dom] / (tot_ms[dom] * 1e-3) / 1e9
-    kernel_names = {"route": "moe_route_kernel", "gateup": "moe_gateup_kernel<8>", "down": "moe_down_kernel<2>",
-                    "combine": "ep_combine_kernel"}
+    step_bytes = sum(sum(b.values()) for b in bytes_per_layer)
+    # The step is ONE kernel launch (moe_step_kernel): achieved = algorithmic
+    # bytes of the step / its CUDA-event duration from the timed loop.
+    achieved = step_bytes / (ms_step * 1e-3) / 1e9
+    kname = f"moe_step_kernel<{H // 256},{I // 256}>"
     traffic = None
     tfile = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tfile):
         try:
-            tj = json.load(open(tfile))
-            traffic = tj.get(f"{kernel_names[dom]}@T{T}")
+            traffic = json.load(open(tfile)).get(f"{kname}@T{T}")
         except Exception:
             traffic = None
-    step_bytes = sum(sum(b.values()) for b in bytes_per_layer)
+    timeline = layer_timeline(stamps)
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -370,12 +392,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "i32+f32", "data": "synthetic",
         "config": config_block(args, world),
-        "roofline": {"bound": "hbm", "kernel": kernel_names[dom], "achieved": achieved, "peak": hbm_peak,
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": hbm_peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": traffic,
-                     "algorithmic_bytes_per_launch": tot_b[dom] / LAYERS,
-                     "avg_launch_us": tot_ms[dom] / LAYERS * 1e3},
-        "kernels_us_per_layer": {n: tot_ms[n] / LAYERS * 1e3 for n in names},
-        "step_hbm_gbs": step_bytes / (ms_step * 1e-3) / 1e9,
+                     "algorithmic_bytes_per_launch": step_bytes, "avg_launch_us": ms_step * 1e3},
+        "phases_us_per_layer": {n: tot_ms[n] / LAYERS * 1e3 for n in names},
+        "layer_timeline": timeline,
         "experts_per_layer": float(np.mean(groups)),
         "cpu_baseline": cpu,
         "e2e": {"value": T / (ms_e2e / args.steps * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": T * H * 4,

@@ -48,6 +48,7 @@ SIGNATURES = {
     "bread_stack_step_host": (_I, [_P, _P, _P, _I, _P]),
     "bread_stack_launches_per_step": (_I, [_P, _I]),
     "bread_stack_profile_step": (_I, [_P, _P, _I, _P, _P]),
+    "bread_stack_profile_stamps": (_I, [_P, _P, _SZ, ctypes.POINTER(_I)]),
     "bread_stack_routing_stats": (_I, [_P, _P, _P]),
     "bread_synth_blocks": (_I, [_P, _LL, _I, _U64, _U64, _P]),
     "bread_synth_normal_f32": (_I, [_P, _LL, _F, _U64, _U64, _P]),

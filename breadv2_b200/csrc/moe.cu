@@ -1,38 +1,41 @@
-// moe.cu -- the MoE FFN block on sm_100a: device router with top-k (K1), one
-// grouped gate/up + SiLU*mul launch over every active expert (K2), one grouped
-// down launch fused with the router-weighted combine (K3), and the
-// expert-parallel combine.
+// moe.cu -- the MoE FFN on sm_100a as ONE persistent, cooperative kernel per
+// call: a whole decode step of L MoE layers (or one MoE block) runs in a
+// single launch of one CTA per SM, with grid-wide barriers between phases
+// instead of kernel boundaries.
 //
 // Reference path replaced: route_layer (one_layer.cu:937-992, with
 // cpu_softmax/cpu_topk layer_ops.cu:222-250), the shared expert
 // (one_layer.cu:1840-1894) and the serial expert loop (one_layer.cu:1931-1983:
 // per expert bread_matvec gate, up, silu_mul_inplace, bread_matvec down,
-// scale_accum).
+// scale_accum), for each of the 40 layers of the decode loop (main.cu:683-687).
 //
-// Data flow for T tokens (all in the caller's workspace):
-//   K1  CTAs of 2 router rows x 4 tokens: quantise a slice of x to int16 (+ per
-//       group sums of squares) and compute their logits (fp32, fixed-order
-//       reduction).  The last CTA to finish (atomic ticket) does softmax and
-//       top-k per token, groups the (token, slot) pairs by expert -- group 0
-//       is the shared expert, then routed experts by ascending id -- and
-//       writes a table of chunks (<= 8 pairs of one expert) holding resolved
-//       weight pointers, tokens and weights, so the expert kernels start
-//       their copies after a single table read.
-//   K2  persistent CTAs walk items (chunk, 32-row tile): a producer warp bulk
-//       copies the chunk record and its tokens' int16 activations, and the 32
-//       gate + 32 up rows in sub-stages; 8 consumer warps compute silu(g)*u
-//       and quantise the 32 results (one activation group) to int16.
-//   K3  CTAs own 16 output rows: the producer streams, per chunk, those rows
-//       of the chunk's down matrix together with the chunk's intermediate;
-//       consumers accumulate w * result per (token, row) in per-warp shared
-//       memory, summed in fixed warp order at the end: deterministic, no
-//       atomics.
-// All kernels are launched with programmatic dependent launch: each one
-// issues the work that does not depend on its predecessor (router rows in K1,
-// shared-expert rows in K2, down rows in K3) before griddepcontrol.wait.
+// Per layer, for T tokens (CTA = 8 consumer warps + 1 producer warp):
+//   A  every CTA quantises a share of the layer input to int16 per 32 values
+//      (plus per-group sums of squares for the RMS norm) and computes its
+//      router rows (fp32 weights already in shared memory, loaded during the
+//      previous layer) -> logits.                          grid barrier
+//   B  every CTA routes all tokens itself from the logits (softmax, top-k
+//      with lowest index winning ties, renormalisation, sigmoid of the shared
+//      gate) and groups the (token, expert) pairs by expert -- the same
+//      deterministic tables in every CTA, no extra barrier.  The producer
+//      then issues, at once, the bulk copies of this CTA's gate/up rows AND
+//      of its down rows (which do not depend on the intermediate), so a
+//      whole layer's expert weights are in flight together.  Consumers
+//      compute silu(g)*u for 32-row items and store it quantised to int16.
+//                                                          grid barrier
+//   C  each CTA owns 16 output columns of h: it adds the router-weighted
+//      down projections of every active expert for them, in fixed order
+//      (deterministic, no atomics), h_out = h_in + sum.     grid barrier
+// Work that does not depend on the routing -- the next layer's router rows
+// and the first shared-expert gate/up rows -- is copied during the previous
+// layer.  With expert parallelism (ep_world > 1) phase C writes the rank's
+// partial columns into every rank's mailbox over NVLink and counts one
+// arrival per column tile there; the next phase A waits (bounded) for all
+// ranks' arrivals and reads h = h_prev + sum of partials in rank order, so
+// every rank holds the same bits and routes identically.
 #include <math.h>
 
-#include <utility>
+#include <mutex>
 
 #include "common.cuh"
 #include "moe.cuh"
@@ -41,57 +44,207 @@
 
 namespace bread {
 
-template <int QT, int NB>
-struct MGeo {
-    static constexpr int BB = QT == BREAD_QTYPE_Q4_K ? Q4K_BYTES : Q6K_BYTES;
-    static constexpr int LANES_ALL = 4 * NB;
-    static constexpr int CP = LANES_ALL > 32 ? LANES_ALL / 32 : 1;
-    static constexpr int LPR = LANES_ALL > 32 ? 32 : LANES_ALL;
-    static constexpr int RPW = 32 / LPR;
-    static constexpr int ROWB = BB * NB;
-    static constexpr int STEPB = ROWB * RPW;
+constexpr int ST_THREADS = 288;  // 8 consumer warps + 1 producer warp
+constexpr int ST_CONS = 256;
+constexpr int BAR_CONS = 1;      // named barrier of the consumer warps
+constexpr int BAR_ALL = 2;       // consumers + producer: routing tables ready
+constexpr size_t SMEM_LIMIT = 232448;  // dynamic shared memory per CTA (227 KB)
+constexpr unsigned long long GRID_WAIT_NS = 2000000000ull;  // 2 s
+constexpr unsigned long long EP_WAIT_NS = 20000000000ull;   // 20 s (peers may start late)
+
+template <int NBH, int NBI>
+struct SCfg {
+    using GH = MGeo<BREAD_QTYPE_Q4_K, NBH>;
+    using GI = MGeo<BREAD_QTYPE_Q6_K, NBI>;
+    static constexpr int H = QK * NBH;
+    static constexpr int I = QK * NBI;
+    static constexpr int SR = 8 * GH::RPW < MOE_ROWTILE ? 8 * GH::RPW : MOE_ROWTILE;  // rows per gate/up sub-stage
+    static constexpr int SPI = MOE_ROWTILE / SR;                                      // sub-stages per item
+    static constexpr int STB = 2 * SR * GH::ROWB;                                     // gate rows + up rows
+    static constexpr int WS = MOE_RT3 / GI::RPW;                                      // warp steps per down stage
+    static constexpr int WB = MOE_RT3 * GI::ROWB;                                     // down weight bytes per stage
+    static constexpr int XTOK = H * 2 + H / 8;  // one token: int16 activations + group scales
+    static constexpr int ATOK = I * 2 + I / 8;  // one pair: int16 intermediate + group scales
 };
 
-constexpr size_t CHUNK_HDR = 128;  // chunk record at the head of a staged slot
+// ---------------------------------------------------------------------------
+// device helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool dev_failed() { return *reinterpret_cast<volatile unsigned *>(&g_dev_error) != 0; }
 
-__host__ __device__ constexpr size_t al16(size_t v) { return (v + 15) / 16 * 16; }
-
-__device__ __forceinline__ float warp_sum(float v)
+// Bounded wait until *p >= target (acquire at gpu or system scope).  Gives up
+// at once when a wait anywhere on the device has already failed, so a lost
+// peer costs one timeout, not one per remaining barrier.
+__device__ bool wait_counter(const unsigned long long *p, unsigned long long target, bool sys,
+                             unsigned long long limit_ns)
 {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
+    unsigned long long t0 = 0;
+    for (unsigned i = 0;; ++i) {
+        const unsigned long long v = sys ? ld_acquire_sys(p) : ld_acquire_gpu(p);
+        if (v >= target) return true;
+        if ((i & 63) == 63) {
+            if (dev_failed()) return false;
+            const unsigned long long now = globaltimer();
+            if (!t0) {
+                t0 = now;
+            } else if (now - t0 > limit_ns) {
+                flag_error(DEVERR_TIMEOUT);
+                return false;
+            }
+        }
+        if (i > 16) __nanosleep(20);
+    }
 }
 
-// ---------------------------------------------------------------------------
-// K1: router + finalize
-// ---------------------------------------------------------------------------
-constexpr int K1_ROWS = 2;                  // router rows per CTA (4 warps per row)
-constexpr int K1_MAXV = MOE_HMAX / 4 / 64;  // float2 per lane of a quarter row
-
-// Runs in the last K1 CTA to finish (256 threads).  It sits between the router
-// GEMV and the expert kernels, so global inputs are read in one round of
-// independent loads and all intermediate state stays in shared memory.
-__device__ void moe_finalize(const MoeArgs &a)
+// Bounded mbarrier wait that also gives up once the device error word is set.
+__device__ __forceinline__ void swait(uint64_t *bar, unsigned parity)
 {
-    __shared__ int s_cnt[MOE_EMAX], s_run[MOE_EMAX], s_off[MOE_EMAX];
-    __shared__ int s_gexp[MOE_EMAX + 1], s_goff[MOE_EMAX + 1], s_gcnt[MOE_EMAX + 1], s_gcpre[MOE_EMAX + 2];
-    __shared__ float s_rinv[MOE_TMAX], s_sgw[MOE_TMAX];
-    __shared__ int s_idx[MOE_TMAX * MOE_KMAX];
-    __shared__ float s_w[MOE_TMAX * MOE_KMAX];
-    __shared__ int s_ptok[MOE_TMAX * (MOE_KMAX + 1)];
-    __shared__ float s_pw[MOE_TMAX * (MOE_KMAX + 1)];
-    __shared__ int s_ng, s_nch, s_np;
+    if (mbar_try_wait(bar, parity)) return;
+    for (long long i = 0; i < SPIN_LIMIT; ++i) {
+        if (mbar_try_wait(bar, parity)) return;
+        if ((i & 1023) == 1023 && dev_failed()) return;
+        if (i > 64) __nanosleep(32);
+    }
+    flag_error(DEVERR_TIMEOUT);
+}
+
+// Grid-wide barrier number `idx` of this launch (all 256 consumer threads).
+__device__ __forceinline__ void grid_barrier(const StepArgs &a, int idx, int tid)
+{
+    named_sync(BAR_CONS, ST_CONS);
+    if (tid == 0) {
+        __threadfence();
+        atomicAdd(a.ctrl + CTRL_GRID, 1ull);
+        wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(idx + 1) * gridDim.x, false, GRID_WAIT_NS);
+    }
+    named_sync(BAR_CONS, ST_CONS);
+}
+
+__device__ __forceinline__ StepLayer layer_desc(const StepArgs &a, int l) { return a.layers ? a.layers[l] : a.l0; }
+__device__ __forceinline__ const float *in_of(const StepArgs &a, int l) { return l == 0 ? a.x : a.buf[l & 1]; }
+__device__ __forceinline__ float *out_of(const StepArgs &a, int l) { return l == a.L - 1 ? a.y : a.buf[(l + 1) & 1]; }
+
+// Mailbox slot of layer l's partials.  Consecutive layers, and the last layer
+// of a step and the first of the next, always use different slots; with the
+// chained waits that makes a slot safe to rewrite.
+__device__ __forceinline__ int ep_slot(int L, int l) { return ((L & 1) && l == L - 1) ? 2 : (l & 1); }
+// Arrival count that completes layer l's partials in launch `epoch`.
+__device__ __forceinline__ unsigned long long ep_target(const StepArgs &a, int l, unsigned long long epoch, int NT)
+{
+    const int s = ep_slot(a.L, l);
+    const unsigned long long uses = s == 2 ? 1ull : (unsigned long long)(a.L / 2);
+    const unsigned long long u = s == 2 ? 0ull : (unsigned long long)(l >> 1);
+    return (epoch * uses + u + 1) * (unsigned long long)a.ep_world * (unsigned long long)NT;
+}
+// Float offset of a mailbox slot's partials (rank r's start r * ep_tmax * H later).
+__device__ __forceinline__ size_t mb_slot_off(int slot, const StepArgs &a)
+{
+    return StepMailbox::data_off(slot, 0, a.ep_world, a.ep_tmax, a.H) / 4;
+}
+__device__ __forceinline__ unsigned long long *ep_counter(const StepArgs &a, int rank, int slot)
+{
+    const StepMailbox M = StepMailbox::make(a.ep_world, a.ep_tmax, a.H);
+    return reinterpret_cast<unsigned long long *>(reinterpret_cast<uint8_t *>(a.ep_mb[rank]) + M.ctr_off) + slot;
+}
+
+__device__ __forceinline__ const uint8_t *expert_ptr(const uint8_t *const *tab, const uint8_t *sh, int e, int E)
+{
+    if (e >= E) return sh;
+    return reinterpret_cast<const uint8_t *>(__ldg(reinterpret_cast<const unsigned long long *>(tab + e)));
+}
+
+// Routing tables of one layer, in shared memory (identical in every CTA).
+struct RouteTabs {
+    int *idx;
+    float *w, *rinv, *sgw;
+    int *cnt, *run, *off, *gexp, *goff, *gcnt, *gcpre, *ptok;
+    float *pw;
+    int *scal;             // [0] groups, [1] chunks, [2] pairs
+    const uint8_t **ptr;   // [EL][3]: gate, up, down of each routed expert used here
+    int4 *chunk;           // [chunks]: expert, first pair, pairs
+};
+
+struct ChunkInfo {
+    int e, p0, np;
+};
+
+// Cursor of a ring of `ns` shared-memory stages: the slot, the parity of its
+// current use, and whether the slot was used before (then its "empty" barrier
+// of the previous use is awaited before refilling).  Advanced incrementally:
+// no division on the per-copy path of the single producer thread.
+struct Ring {
+    int slot = 0, phase = 0, used = 0;
+    __device__ __forceinline__ void next(int ns)
+    {
+        if (++slot == ns) {
+            slot = 0;
+            phase ^= 1;
+            used = 1;
+        }
+    }
+};
+
+// Matrix k (0 gate, 1 up, 2 down) of expert e (E = the shared expert).
+__device__ __forceinline__ const uint8_t *mat_ptr(const RouteTabs &R, const StepLayer &Ld, const StepArgs &a, int e,
+                                                  int k)
+{
+    if (e >= a.E) return k == 0 ? Ld.sh_gate : k == 1 ? Ld.sh_up : Ld.sh_down;
+    if (Ld.gate_base) {
+        const size_t j = (size_t)(e - a.lo);
+        return k == 0 ? Ld.gate_base + j * Ld.gu_stride : k == 1 ? Ld.up_base + j * Ld.gu_stride
+                                                                 : Ld.down_base + j * Ld.d_stride;
+    }
+    return R.ptr[3 * (e - a.lo) + k];
+}
+
+// Chunk c: up to MOE_TC consecutive pairs of one expert group (from the
+// table built with the routing).
+__device__ __forceinline__ ChunkInfo chunk_info(const RouteTabs &R, int c)
+{
+    const int4 v = R.chunk[c];
+    ChunkInfo ci;
+    ci.e = v.x;
+    ci.p0 = v.y;
+    ci.np = v.z;
+    return ci;
+}
+
+// Chunk c looked up from the group tables (binary search over groups).
+__device__ __forceinline__ ChunkInfo chunk_search(const RouteTabs &R, int c)
+{
+    int lo = 0, hi = R.scal[0] - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (R.gcpre[mid] <= c)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    const int k = c - R.gcpre[lo];
+    ChunkInfo ci;
+    ci.e = R.gexp[lo];
+    ci.p0 = R.goff[lo] + MOE_TC * k;
+    ci.np = min(MOE_TC, R.gcnt[lo] - MOE_TC * k);
+    return ci;
+}
+
+// Phase B routing, run by the 256 consumer threads of every CTA from the
+// logits in global memory: softmax + top-k (layer_ops.cu:222-250) with the
+// RMS factor of the token applied to the logits, renormalised weights, the
+// shared gate's sigmoid (0.5 without a gate vector, one_layer.cu:944,1889),
+// then the (token, expert) pairs grouped by expert: group 0 is the shared
+// expert (all T tokens), then the routed experts held here by ascending id,
+// pairs token-major inside each group.
+template <int PER>
+__device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const RouteTabs &R, int l, bool cta0)
+{
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = a.T, H = a.H, E = a.E, K = a.top_k, HG = H / 32;
-    for (int i = tid; i < MOE_EMAX; i += blockDim.x) {
-        s_cnt[i] = 0;
-        s_run[i] = 0;
+    const int EL = a.hi - a.lo;
+    for (int i = tid; i < EL; i += ST_CONS) {
+        R.cnt[i] = 0;
+        R.run[i] = 0;
     }
-
-    // (a) per token (one warp each): RMS factor, softmax, top-k
-    //     (layer_ops.cu:222-250), renormalised weights, shared-gate sigmoid
-    constexpr int PER = MOE_EMAX / 32;
     for (int t = warp; t < T; t += 8) {
         float p[PER];
 #pragma unroll
@@ -101,7 +254,7 @@ __device__ void moe_finalize(const MoeArgs &a)
         }
         float ss = 0.0f;
         for (int g = lane; g < HG; g += 32) ss += __ldcg(a.ssq + t * HG + g);
-        const float score = __ldcg(a.score + t);
+        const float score = Ld.w_sg ? __ldcg(a.score + t) : 0.0f;
         ss = warp_sum(ss);
         const float r = a.norm_eps >= 0.0f ? rsqrtf(ss / (float)H + a.norm_eps) : 1.0f;
         float m = -INFINITY;
@@ -151,47 +304,141 @@ __device__ void moe_finalize(const MoeArgs &a)
         }
         if (lane < K) {
             const float w = wsum > 0.0f ? my_w / wsum : my_w;
-            s_idx[t * K + lane] = my_i;
-            s_w[t * K + lane] = w;
-            a.ridx[t * K + lane] = my_i;
-            a.rw[t * K + lane] = w;
-            if (a.idx_out) a.idx_out[t * K + lane] = my_i;
-            if (a.w_out) a.w_out[t * K + lane] = w;
+            R.idx[t * K + lane] = my_i;
+            R.w[t * K + lane] = w;
+            if (cta0 && a.idx_out) a.idx_out[t * K + lane] = my_i;
+            if (cta0 && a.w_out) a.w_out[t * K + lane] = w;
         }
         if (lane == 0) {
-            const float sg = a.w_sg ? 1.0f / (1.0f + expf(-(score * r))) : 0.5f;
-            s_rinv[t] = r;
-            s_sgw[t] = sg;
-            a.sgw[t] = sg;
-            if (a.sg_out) a.sg_out[t] = sg;
+            const float sg = Ld.w_sg ? 1.0f / (1.0f + expf(-(score * r))) : 0.5f;
+            R.rinv[t] = r;
+            R.sgw[t] = sg;
+            if (cta0 && a.sg_out) a.sg_out[t] = sg;
         }
     }
-    __syncthreads();
+    named_sync(BAR_CONS, ST_CONS);
+    if (a.route_only) return;
 
-    // (b) scales of the normalised activations; pairs per local expert
-    if (a.norm_eps >= 0.0f)
-        for (int i = tid; i < T * HG; i += blockDim.x) a.xs[i] = __ldcg(a.xs + i) * s_rinv[i / HG];
     const int P = T * K;
-    for (int q = tid; q < P; q += blockDim.x) {
-        const int e = s_idx[q];
-        if (e >= a.lo && e < a.hi) atomicAdd(&s_cnt[e - a.lo], 1);
+    if (P <= 32) {
+        // Few pairs (decode): one warp ranks them directly.  Lane q holds pair
+        // q = (token q / K, slot q % K); same tables as the general path below.
+        if (warp == 0) {
+            const int hs = Ld.sh_gate ? 1 : 0;
+            const int hsc = hs ? (T + MOE_TC - 1) / MOE_TC : 0;
+            const int pb = hs ? T : 0;
+            int e = 0x7fffffff;
+            float w = 0.0f;
+            bool loc = false;
+            if (lane < P) {
+                const int ee = R.idx[lane];
+                if (ee >= a.lo && ee < a.hi) {
+                    e = ee;
+                    w = R.w[lane];
+                    loc = true;
+                }
+            }
+            int before = 0;  // earlier pairs of the same expert
+            for (int j = 0; j < P; ++j) before += (__shfl_sync(0xffffffffu, e, j) == e && j < lane) ? 1 : 0;
+            const bool first = loc && before == 0;
+            int less = 0, dless = 0, same = 0;
+            for (int j = 0; j < P; ++j) {
+                const int ej = __shfl_sync(0xffffffffu, e, j);
+                const int fj = __shfl_sync(0xffffffffu, first ? 1 : 0, j);
+                less += ej < e ? 1 : 0;
+                dless += (ej < e && fj) ? 1 : 0;
+                same += ej == e ? 1 : 0;
+            }
+            const int chn = first ? (same + MOE_TC - 1) / MOE_TC : 0;
+            int cpre = 0;
+            for (int j = 0; j < P; ++j) {
+                const int ej = __shfl_sync(0xffffffffu, e, j);
+                const int cj = __shfl_sync(0xffffffffu, chn, j);
+                cpre += ej < e ? cj : 0;
+            }
+            if (loc) {
+                const int pos = pb + less + before;
+                R.ptok[pos] = lane / K;
+                R.pw[pos] = w;
+                if (first) {
+                    const int g = hs + dless;
+                    R.gexp[g] = e;
+                    R.goff[g] = pb + less;
+                    R.gcnt[g] = same;
+                    R.gcpre[g] = hsc + cpre;
+                    for (int k = 0; k < chn; ++k)
+                        R.chunk[hsc + cpre + k] = make_int4(e, pb + less + MOE_TC * k, min(MOE_TC, same - MOE_TC * k), 0);
+                    if (!Ld.gate_base) {
+                        R.ptr[3 * (e - a.lo) + 0] = expert_ptr(Ld.gate, nullptr, e, E);
+                        R.ptr[3 * (e - a.lo) + 1] = expert_ptr(Ld.up, nullptr, e, E);
+                        R.ptr[3 * (e - a.lo) + 2] = expert_ptr(Ld.down, nullptr, e, E);
+                    }
+                }
+            }
+            const int ngr = __popc(__ballot_sync(0xffffffffu, first));
+            const int npl = __popc(__ballot_sync(0xffffffffu, loc));
+            int nchr = chn;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) nchr += __shfl_xor_sync(0xffffffffu, nchr, o);
+            if (hs) {
+                for (int t = lane; t < T; t += 32) {
+                    R.ptok[t] = t;
+                    R.pw[t] = R.sgw[t];
+                }
+                for (int k = lane; k < hsc; k += 32) R.chunk[k] = make_int4(E, MOE_TC * k, min(MOE_TC, T - MOE_TC * k), 0);
+            }
+            if (lane == 0) {
+                if (hs) {
+                    R.gexp[0] = E;
+                    R.goff[0] = 0;
+                    R.gcnt[0] = T;
+                    R.gcpre[0] = 0;
+                }
+                const int ng = hs + ngr;
+                R.gcpre[ng] = hsc + nchr;
+                R.scal[0] = ng;
+                R.scal[1] = hsc + nchr;
+                R.scal[2] = pb + npl;
+                if (cta0 && a.stats) {
+                    a.stats[2 * l] = ng;
+                    a.stats[2 * l + 1] = pb + npl;
+                }
+            }
+        }
+        named_sync(BAR_CONS, ST_CONS);
+        return;
     }
-    __syncthreads();
 
-    // (c) one warp: groups (shared expert first, then routed experts by id),
-    //     chunk prefix, pair placement (token-major inside each expert)
+    for (int q = tid; q < P; q += ST_CONS) {
+        const int e = R.idx[q];
+        if (e >= a.lo && e < a.hi) atomicAdd(&R.cnt[e - a.lo], 1);
+    }
+    named_sync(BAR_CONS, ST_CONS);
+
+    // warps 1..7: weight pointers of every expert used here, all loads in
+    // flight together (the producer would otherwise chase them one by one)
+    if (warp > 0 && !Ld.gate_base)
+        for (int el = tid - 32; el < EL; el += ST_CONS - 32)
+            if (R.cnt[el]) {
+                const int e = a.lo + el;
+                const uint8_t *g = expert_ptr(Ld.gate, nullptr, e, E);
+                const uint8_t *u = expert_ptr(Ld.up, nullptr, e, E);
+                const uint8_t *d = expert_ptr(Ld.down, nullptr, e, E);
+                R.ptr[3 * el + 0] = g;
+                R.ptr[3 * el + 1] = u;
+                R.ptr[3 * el + 2] = d;
+            }
     if (warp == 0) {
-        const int NL = a.hi - a.lo;
-        const int hs = a.shared_here ? 1 : 0;
+        const int hs = Ld.sh_gate ? 1 : 0;
         int gbase = hs, pbase = hs ? T : 0;
         if (hs && lane == 0) {
-            s_gexp[0] = E;
-            s_goff[0] = 0;
-            s_gcnt[0] = T;
+            R.gexp[0] = E;
+            R.goff[0] = 0;
+            R.gcnt[0] = T;
         }
-        for (int c0 = 0; c0 < NL; c0 += 32) {
+        for (int c0 = 0; c0 < EL; c0 += 32) {
             const int el = c0 + lane;
-            const int cnt = el < NL ? s_cnt[el] : 0;
+            const int cnt = el < EL ? R.cnt[el] : 0;
             const int flag = cnt > 0 ? 1 : 0;
             int fi = flag, ci = cnt;
 #pragma unroll
@@ -205,11 +452,11 @@ __device__ void moe_finalize(const MoeArgs &a)
             }
             const int gid = gbase + fi - flag, off = pbase + ci - cnt;
             if (flag) {
-                s_gexp[gid] = a.lo + el;
-                s_goff[gid] = off;
-                s_gcnt[gid] = cnt;
+                R.gexp[gid] = a.lo + el;
+                R.goff[gid] = off;
+                R.gcnt[gid] = cnt;
             }
-            if (el < NL) s_off[el] = off;
+            if (el < EL) R.off[el] = off;
             gbase += __shfl_sync(0xffffffffu, fi, 31);
             pbase += __shfl_sync(0xffffffffu, ci, 31);
         }
@@ -218,14 +465,14 @@ __device__ void moe_finalize(const MoeArgs &a)
         int cbase = 0;
         for (int g0 = 0; g0 < ng; g0 += 32) {
             const int g = g0 + lane;
-            const int ch = g < ng ? (s_gcnt[g] + MOE_TC - 1) / MOE_TC : 0;
+            const int ch = g < ng ? (R.gcnt[g] + MOE_TC - 1) / MOE_TC : 0;
             int ci = ch;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const int c = __shfl_up_sync(0xffffffffu, ci, o);
                 if (lane >= o) ci += c;
             }
-            if (g < ng) s_gcpre[g] = cbase + ci - ch;
+            if (g < ng) R.gcpre[g] = cbase + ci - ch;
             cbase += __shfl_sync(0xffffffffu, ci, 31);
         }
         for (int q0 = 0; q0 < P; q0 += 32) {
@@ -233,7 +480,7 @@ __device__ void moe_finalize(const MoeArgs &a)
             int e = -1;
             bool loc = false;
             if (q < P) {
-                e = s_idx[q];
+                e = R.idx[q];
                 loc = e >= a.lo && e < a.hi;
             }
             const unsigned act = __ballot_sync(0xffffffffu, loc);
@@ -241,558 +488,522 @@ __device__ void moe_finalize(const MoeArgs &a)
                 const unsigned peers = __match_any_sync(act, e);
                 const int rank = __popc(peers & ((1u << lane) - 1u));
                 const int el = e - a.lo;
-                const int pos = s_off[el] + s_run[el] + rank;
-                s_ptok[pos] = q / K;
-                s_pw[pos] = s_w[q];
-                if (__ffs(peers) - 1 == lane) s_run[el] += __popc(peers);
+                const int pos = R.off[el] + R.run[el] + rank;
+                R.ptok[pos] = q / K;
+                R.pw[pos] = R.w[q];
+                if (__ffs(peers) - 1 == lane) R.run[el] += __popc(peers);
             }
             __syncwarp();
         }
         if (hs)
             for (int t = lane; t < T; t += 32) {
-                s_ptok[t] = t;
-                s_pw[t] = s_sgw[t];
+                R.ptok[t] = t;
+                R.pw[t] = R.sgw[t];
             }
         if (lane == 0) {
-            s_gcpre[ng] = cbase;
-            s_ng = ng;
-            s_nch = cbase;
-            s_np = pbase;
-        }
-    }
-    __syncthreads();
-
-    // (d) all threads: pair lists and the chunk table
-    const int ng = s_ng, nch = s_nch, np_tot = s_np;
-    for (int p = tid; p < np_tot; p += blockDim.x) {
-        a.p_token[p] = s_ptok[p];
-        a.p_w[p] = s_pw[p];
-    }
-    // (route-only calls have no expert tables and need no chunk table)
-    for (int c = tid; a.gate && c < nch; c += blockDim.x) {
-        int lo = 0, hi = ng - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (s_gcpre[mid] <= c)
-                lo = mid;
-            else
-                hi = mid - 1;
-        }
-        const int g = lo, ci = c - s_gcpre[g], e = s_gexp[g];
-        MoeChunk ch;
-        ch.gate = e >= E ? a.sh_gate : a.gate[e];
-        ch.up = e >= E ? a.sh_up : a.up[e];
-        ch.down = e >= E ? a.sh_down : a.down[e];
-        ch.p0 = s_goff[g] + MOE_TC * ci;
-        ch.np = min(MOE_TC, s_gcnt[g] - MOE_TC * ci);
-        ch.group = g;
-        ch.pad = 0;
-#pragma unroll
-        for (int j = 0; j < MOE_TC; ++j) {
-            ch.tok[j] = (uint8_t)(j < ch.np ? s_ptok[ch.p0 + j] : 0);
-            ch.w[j] = j < ch.np ? s_pw[ch.p0 + j] : 0.0f;
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ch.pad2[j] = 0;
-        const uint4 *src = reinterpret_cast<const uint4 *>(&ch);
-        uint4 *dst = reinterpret_cast<uint4 *>(a.chunks + c);
-#pragma unroll
-        for (int j = 0; j < (int)(sizeof(MoeChunk) / 16); ++j) dst[j] = src[j];
-    }
-    if (tid == 0) {
-        a.hdr[HDR_NGROUPS] = ng;
-        a.hdr[HDR_NCHUNKS] = nch;
-        a.hdr[HDR_NPAIRS] = np_tot;
-        if (a.stats) {
-            a.stats[0] = ng;
-            a.stats[1] = np_tot;
-        }
-        a.hdr[HDR_TICKET] = 0;  // re-armed for the next launch
-    }
-}
-
-__global__ void __launch_bounds__(256) moe_route_kernel(MoeArgs a)
-{
-    __shared__ float s_part[K1_ROWS][4][K1_TG];
-    __shared__ int s_last;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int T = a.T, H = a.H, E = a.E;
-    const int nrows = E + (a.w_sg ? 1 : 0);
-    const int rl = warp >> 2, qt = warp & 3;
-    const int row = blockIdx.x * K1_ROWS + rl;
-    const int seg = H >> 2, nv = seg >> 6;  // float2 per lane
-    const int c0 = qt * seg + 2 * lane;
-
-    // The router row does not depend on the previous kernel: load it first.
-    float2 wv[K1_MAXV];
-#pragma unroll
-    for (int j = 0; j < K1_MAXV; ++j) {
-        wv[j] = make_float2(0.0f, 0.0f);
-        if (j < nv && row < nrows) {
-            const int c = c0 + 64 * j;
-            if (row < E)
-                wv[j] = *reinterpret_cast<const float2 *>(a.W_r + (size_t)row * H + c);
-            else
-                wv[j] = __half22float2(*reinterpret_cast<const __half2 *>(a.w_sg + c));
-        }
-    }
-    pdl_wait();
-    pdl_launch_dependents();
-
-    // quantise x: T*H/32 groups over all warps of the grid
-    {
-        const int groups = T * (H / 32);
-        const int nw = gridDim.x * gridDim.y * 8;
-        for (int gi = (blockIdx.y * gridDim.x + blockIdx.x) * 8 + warp; gi < groups; gi += nw) {
-            const float v = a.x[(size_t)gi * 32 + lane];
-            const float ss = warp_sum(v * v);
-            if (lane == 0) a.ssq[gi] = ss;
-            const int q = quant32(v, a.xs + gi, lane);
-            a.xq[(size_t)gi * 32 + lane] = (int16_t)q;
-        }
-    }
-    // logits of this CTA's rows for its tokens, two tokens per pass
-    const int t0 = blockIdx.y * K1_TG;
-    const int tn = min(K1_TG, T - t0);
-    if (row < nrows) {
-        for (int tl = 0; tl < tn; tl += 2) {
-            const bool two = tl + 1 < tn;
-            const float *x0 = a.x + (size_t)(t0 + tl) * H;
-            const float *x1 = two ? x0 + H : x0;
-            float2 xa[K1_MAXV], xb[K1_MAXV];
-#pragma unroll
-            for (int j = 0; j < K1_MAXV; ++j)
-                if (j < nv) {
-                    xa[j] = *reinterpret_cast<const float2 *>(x0 + c0 + 64 * j);
-                    xb[j] = *reinterpret_cast<const float2 *>(x1 + c0 + 64 * j);
-                }
-            float s0 = 0.0f, s1 = 0.0f;
-#pragma unroll
-            for (int j = 0; j < K1_MAXV; ++j)
-                if (j < nv) {
-                    s0 = fmaf(wv[j].x, xa[j].x, s0);
-                    s0 = fmaf(wv[j].y, xa[j].y, s0);
-                    s1 = fmaf(wv[j].x, xb[j].x, s1);
-                    s1 = fmaf(wv[j].y, xb[j].y, s1);
-                }
-            s0 = warp_sum(s0);
-            s1 = warp_sum(s1);
-            if (lane == 0) {
-                s_part[rl][qt][tl] = s0;
-                if (two) s_part[rl][qt][tl + 1] = s1;
+            R.gcpre[ng] = cbase;
+            R.scal[0] = ng;
+            R.scal[1] = cbase;
+            R.scal[2] = pbase;
+            if (cta0 && a.stats) {
+                a.stats[2 * l] = ng;
+                a.stats[2 * l + 1] = pbase;
             }
         }
     }
-    __syncthreads();
-    for (int i = tid; i < K1_ROWS * tn; i += blockDim.x) {
-        const int r_l = i / tn, tl = i % tn;
-        const int rr = blockIdx.x * K1_ROWS + r_l;
-        if (rr < nrows) {
-            const float v = ((s_part[r_l][0][tl] + s_part[r_l][1][tl]) + s_part[r_l][2][tl]) + s_part[r_l][3][tl];
-            if (rr < E)
-                a.logits[(size_t)(t0 + tl) * E + rr] = v;
-            else
-                a.score[t0 + tl] = v;
-        }
+    named_sync(BAR_CONS, ST_CONS);
+    for (int c = tid; c < R.scal[1]; c += ST_CONS) {
+        const ChunkInfo ci = chunk_search(R, c);
+        R.chunk[c] = make_int4(ci.e, ci.p0, ci.np, 0);
     }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const unsigned total = gridDim.x * gridDim.y;
-        const unsigned prev = atomicAdd(reinterpret_cast<unsigned *>(a.hdr + HDR_TICKET), 1u);
-        s_last = prev == total - 1;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    moe_finalize(a);
+    named_sync(BAR_CONS, ST_CONS);
 }
 
 // ---------------------------------------------------------------------------
-// K2: gate/up + SiLU*mul
+// the step kernel
 // ---------------------------------------------------------------------------
-template <int NB>
-struct K2Cfg {
-    using G = MGeo<BREAD_QTYPE_Q4_K, NB>;
-    static constexpr int H = QK * NB;
-    static constexpr int SR = 8 * G::RPW < MOE_ROWTILE ? 8 * G::RPW : MOE_ROWTILE;  // rows per sub-stage
-    static constexpr int SPI = MOE_ROWTILE / SR;                                      // sub-stages per item
-    static constexpr int STB = 2 * SR * G::ROWB;                                      // gate rows + up rows
-    static constexpr int NS = NB >= 16 ? 2 : 4;                                       // weight sub-stage ring
-    static constexpr size_t X_OFF = (size_t)NS * STB;
-    // activation slot: chunk record, then up to 8 token rows of int16, then their scales
-    __host__ __device__ static int tc(int T) { return T < MOE_TC ? T : MOE_TC; }
-    __host__ __device__ static size_t xslot(int T) { return al16(CHUNK_HDR + (size_t)tc(T) * (H * 2 + H / 8)); }
-    __host__ __device__ static size_t bar_off(int T) { return X_OFF + 2 * xslot(T) + 16; }
-    __host__ __device__ static size_t abuf_off(int T) { return bar_off(T) + (size_t)(2 * NS + 4) * 8; }
-    __host__ __device__ static size_t smem(int T) { return abuf_off(T) + MOE_TC * MOE_ROWTILE * 4; }
-};
-
-template <int NB>
-__global__ void __launch_bounds__(288) moe_gateup_kernel(MoeArgs a)
+template <int NBH, int NBI>
+__global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_constant__ StepArgs a)
 {
-    using C = K2Cfg<NB>;
-    using G = typename C::G;
-    constexpr int H = C::H;
+    using C = SCfg<NBH, NBI>;
+    using GH = typename C::GH;
+    using GI = typename C::GI;
+    constexpr int H = C::H, I = C::I;
     extern __shared__ __align__(128) uint8_t smem[];
-    const int T = a.T;
-    const int TC = C::tc(T);
-    const size_t XSLOT = C::xslot(T);
-    uint8_t *wst = smem;
-    uint8_t *xst = smem + C::X_OFF;
-    uint64_t *wfull = reinterpret_cast<uint64_t *>(smem + C::bar_off(T));
-    uint64_t *wempty = wfull + C::NS;
-    uint64_t *xfull = wempty + C::NS;
-    uint64_t *xempty = xfull + 2;
-    float *abuf = reinterpret_cast<float *>(smem + C::abuf_off(T));
+    const StepSmem &m = a.sm;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int R = a.I / MOE_ROWTILE;
+    const int G = gridDim.x, bx = blockIdx.x;
+    const int T = a.T, E = a.E;
+    const int TC = T < MOE_TC ? T : MOE_TC;
+    const int R = I / MOE_ROWTILE;  // gate/up row tiles per expert
+    const int NT = H / MOE_RT3;     // 16-column tiles of h (down output)
+    const bool ep = a.ep_world > 1;
+    const bool norm = a.norm_eps >= 0.0f;
+    const int NS_G = m.NS_G, NS_D = m.NS_D;
+
+    float *rbuf = reinterpret_cast<float *>(smem + m.rbuf);
+    float *part = reinterpret_cast<float *>(smem + m.part);
+    RouteTabs RT;
+    RT.idx = reinterpret_cast<int *>(smem + m.r_idx);
+    RT.w = reinterpret_cast<float *>(smem + m.r_w);
+    RT.rinv = reinterpret_cast<float *>(smem + m.r_rinv);
+    RT.sgw = reinterpret_cast<float *>(smem + m.r_sgw);
+    RT.cnt = reinterpret_cast<int *>(smem + m.r_cnt);
+    RT.run = reinterpret_cast<int *>(smem + m.r_run);
+    RT.off = reinterpret_cast<int *>(smem + m.r_off);
+    RT.gexp = reinterpret_cast<int *>(smem + m.r_gexp);
+    RT.goff = reinterpret_cast<int *>(smem + m.r_goff);
+    RT.gcnt = reinterpret_cast<int *>(smem + m.r_gcnt);
+    RT.gcpre = reinterpret_cast<int *>(smem + m.r_gcpre);
+    RT.ptok = reinterpret_cast<int *>(smem + m.r_ptok);
+    RT.pw = reinterpret_cast<float *>(smem + m.r_pw);
+    RT.scal = reinterpret_cast<int *>(smem + m.r_scal);
+    RT.ptr = reinterpret_cast<const uint8_t **>(smem + m.r_ptr);
+    RT.chunk = reinterpret_cast<int4 *>(smem + m.r_chunk);
+    uint8_t *xsl = smem + m.xsl;
+    uint8_t *gring = smem + m.gring;
+    float *abuf = reinterpret_cast<float *>(smem + m.abuf);
+    uint8_t *dring = smem + m.dring;
+    float *acc = reinterpret_cast<float *>(smem + m.acc);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + m.bars);
+    uint64_t *rbar = bars;
+    uint64_t *gfull = bars + 1, *gempty = gfull + NS_G;
+    uint64_t *xfull = gempty + NS_G, *xempty = xfull + 2;
+    uint64_t *dw = xempty + 2, *da = dw + NS_D, *dempty = da + NS_D;
+
     if (tid == 0) {
-        for (int s = 0; s < C::NS; ++s) {
-            mbar_init(wfull + s, 1);
-            mbar_init(wempty + s, 8);
+        mbar_init(rbar, 1);
+        for (int s = 0; s < NS_G; ++s) {
+            mbar_init(gfull + s, 1);
+            mbar_init(gempty + s, 8);
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(xfull + s, 1);
             mbar_init(xempty + s, 8);
         }
+        for (int s = 0; s < NS_D; ++s) {
+            mbar_init(dw + s, 1);
+            mbar_init(da + s, 1);
+            mbar_init(dempty + s, C::WS);
+        }
         fence_mbar_init();
     }
+    for (int i = tid; i < 8 * T * MOE_RT3; i += ST_THREADS) acc[i] = 0.0f;
     __syncthreads();
+    const unsigned long long epoch = __ldcg(a.ctrl + CTRL_EPOCH);
 
-    if (warp == 8) {  // producer
-        if (lane != 0) return;
-        // The shared expert's chunks come first (chunks 0 .. ceil(T/8)-1 are
-        // group 0), so the first item's weight rows are known before the
-        // router has finished: stream them before waiting on it.
-        const long long sh_items = a.shared_here ? (long long)((T + MOE_TC - 1) / MOE_TC) * R : 0;
-        const long long it0 = blockIdx.x;
-        const bool pre = it0 < sh_items;
-        constexpr int NPRE = C::SPI < C::NS ? C::SPI : C::NS;  // sub-stages that fit the ring
-        if (pre) {
-            const size_t r0 = (size_t)(it0 % R) * MOE_ROWTILE;
-            for (int s = 0; s < NPRE; ++s) {
-                const unsigned bytes = (unsigned)(C::SR * G::ROWB);
-                mbar_arrive_expect_tx(wfull + s, 2 * bytes);
-                bulk_g2s(wst + (size_t)s * C::STB, a.sh_gate + (r0 + (size_t)s * C::SR) * G::ROWB, bytes, wfull + s);
-                bulk_g2s(wst + (size_t)s * C::STB + bytes, a.sh_up + (r0 + (size_t)s * C::SR) * G::ROWB, bytes,
-                         wfull + s);
+    if (warp == 8) {
+        // ================================================================ producer
+        const bool P0 = lane == 0;
+        Ring gR, dR;   // gate/up and down rings, continued across layers
+        int nX = 0;    // activation slots used (2 slots)
+        auto pstamp = [&](int l, int k) { a.stamps[((size_t)l * G + bx) * STAMPS + k] = globaltimer(); };
+        // Router rows of layer l (and the shared-gate vector as row E) -> rbuf.
+        auto issue_router = [&](int l) {
+            const StepLayer Ld = layer_desc(a, l);
+            unsigned bytes = 0;
+            for (int rl = 0; rl < m.RR; ++rl) {
+                const int r = bx * m.RR + rl;
+                bytes += r < E ? H * 4 : (r == E && Ld.w_sg ? H * 2 : 0);
             }
+            if (!bytes) {
+                mbar_arrive(rbar);
+                return;
+            }
+            mbar_arrive_expect_tx(rbar, bytes);
+            for (int rl = 0; rl < m.RR; ++rl) {
+                const int r = bx * m.RR + rl;
+                if (r < E)
+                    bulk_g2s(rbuf + (size_t)rl * H, Ld.W_r + (size_t)r * H, H * 4, rbar);
+                else if (r == E && Ld.w_sg)
+                    bulk_g2s(rbuf + (size_t)rl * H, Ld.w_sg, H * 2, rbar);
+            }
+        };
+        // One gate/up sub-stage (SR gate rows + SR up rows from row r0) at the
+        // ring cursor g.
+        auto issue_gu = [&](Ring &g, const uint8_t *gb, const uint8_t *ub, size_t r0) {
+            if (g.used) swait(gempty + g.slot, (unsigned)(g.phase ^ 1));
+            const unsigned bytes = (unsigned)(C::SR * GH::ROWB);
+            uint8_t *dst = gring + (size_t)g.slot * C::STB;
+            if (gb && ub && !((reinterpret_cast<uintptr_t>(gb) | reinterpret_cast<uintptr_t>(ub)) & 15)) {
+                mbar_arrive_expect_tx(gfull + g.slot, 2 * bytes);
+                bulk_g2s(dst, gb + r0 * GH::ROWB, bytes, gfull + g.slot);
+                bulk_g2s(dst + bytes, ub + r0 * GH::ROWB, bytes, gfull + g.slot);
+            } else {
+                flag_error(DEVERR_ROUTE);
+                mbar_arrive(gfull + g.slot);
+            }
+            g.next(NS_G);
+        };
+        // The shared expert's pairs are the first chunks of every layer, so a
+        // CTA whose first item is a shared one knows its rows before routing:
+        // copy its first sub-stages at the next ring positions (ring drained).
+        auto preissue_shared = [&](int l) -> int {
+            const StepLayer Ld = layer_desc(a, l);
+            if (a.route_only || !Ld.sh_gate || bx >= ((T + MOE_TC - 1) / MOE_TC) * R) return 0;
+            const int npre = C::SPI < NS_G ? C::SPI : NS_G;
+            Ring g = gR;
+            for (int s = 0; s < npre; ++s)
+                issue_gu(g, Ld.sh_gate, Ld.sh_up, (size_t)(bx % R) * MOE_ROWTILE + (size_t)s * C::SR);
+            return npre;
+        };
+        int npre = 0;
+        if (P0) {
+            issue_router(0);
+            npre = preissue_shared(0);
         }
-        pdl_wait();
-        pdl_launch_dependents();
-        const long long n_items = (long long)__ldcg(a.hdr + HDR_NCHUNKS) * R;
-        int n = 0, i = 0;
-        for (long long it = it0; it < n_items; it += gridDim.x, ++i) {
-            const int c = (int)(it / R), rt = (int)(it % R);
-            const MoeChunk *cp = a.chunks + c;
-            const uint8_t *gb =
-                reinterpret_cast<const uint8_t *>(__ldcg(reinterpret_cast<const unsigned long long *>(&cp->gate)));
-            const uint8_t *ub =
-                reinterpret_cast<const uint8_t *>(__ldcg(reinterpret_cast<const unsigned long long *>(&cp->up)));
-            const int np = __ldcg(&cp->np);
-            const uint2 tk = __ldcg(reinterpret_cast<const uint2 *>(cp->tok));
-            // activations of the chunk's tokens
-            const int xsl = i & 1;
-            if (i >= 2 && !mbar_wait(xempty + xsl, (unsigned)(((i >> 1) - 1) & 1))) return;
-            uint8_t *xb = xst + (size_t)xsl * XSLOT;
-            mbar_arrive_expect_tx(xfull + xsl, (unsigned)(sizeof(MoeChunk) + (size_t)np * (H * 2 + H / 8)));
-            bulk_g2s(xb, cp, sizeof(MoeChunk), xfull + xsl);
-            for (int j = 0; j < np; ++j) {
-                const int t = (int)(((j < 4 ? tk.x : tk.y) >> (8 * (j & 3))) & 0xFFu);
-                bulk_g2s(xb + CHUNK_HDR + (size_t)j * H * 2, a.xq + (size_t)t * H, H * 2, xfull + xsl);
-                bulk_g2s(xb + CHUNK_HDR + (size_t)TC * H * 2 + (size_t)j * (H / 8), a.xs + (size_t)t * (H / 32), H / 8,
-                         xfull + xsl);
-            }
-            // weights, in sub-stages
-            const bool ok = gb && ub && !((reinterpret_cast<uintptr_t>(gb) | reinterpret_cast<uintptr_t>(ub)) & 15);
-            if (!ok) flag_error(DEVERR_ROUTE);
-            for (int s = 0; s < C::SPI; ++s, ++n) {
-                if (pre && it == it0 && s < NPRE) continue;  // already streaming since before the wait
-                const int slot = n % C::NS;
-                if (n >= C::NS && !mbar_wait(wempty + slot, (unsigned)(((n / C::NS) - 1) & 1))) return;
-                const size_t r0 = (size_t)rt * MOE_ROWTILE + (size_t)s * C::SR;
-                const unsigned bytes = (unsigned)(C::SR * G::ROWB);
-                if (ok) {
-                    mbar_arrive_expect_tx(wfull + slot, 2 * bytes);
-                    bulk_g2s(wst + (size_t)slot * C::STB, gb + r0 * G::ROWB, bytes, wfull + slot);
-                    bulk_g2s(wst + (size_t)slot * C::STB + bytes, ub + r0 * G::ROWB, bytes, wfull + slot);
-                } else {
-                    mbar_arrive(wfull + slot);
+        for (int l = 0; l < a.L; ++l) {
+            named_sync(BAR_ALL, ST_THREADS);  // routing tables of layer l are ready
+            if (a.route_only) break;
+            if (P0) {
+                if (a.stamps) pstamp(l, 10);
+                const StepLayer Ld = layer_desc(a, l);
+                fence_proxy_async_global();
+                const int nch = RT.scal[1];
+                // gate/up items (chunk c, row tile rt): activations of the
+                // chunk's tokens + 32 gate and up rows in sub-stages
+                for (int it = bx; it < nch * R; it += G, ++nX) {
+                    const int c = it / R, rt = it % R;  // R: a power of two
+                    const ChunkInfo ci = chunk_info(RT, c);
+                    const int xs_ = nX & 1;
+                    if (nX >= 2) swait(xempty + xs_, (unsigned)(((nX >> 1) - 1) & 1));
+                    uint8_t *xb = xsl + (size_t)xs_ * m.xslot;
+                    mbar_arrive_expect_tx(xfull + xs_, (unsigned)(ci.np * C::XTOK));
+                    for (int j = 0; j < ci.np; ++j) {
+                        const int t = RT.ptok[ci.p0 + j];
+                        bulk_g2s(xb + (size_t)j * H * 2, a.xq + (size_t)t * H, H * 2, xfull + xs_);
+                        bulk_g2s(xb + (size_t)TC * H * 2 + (size_t)j * (H / 8), a.xs + (size_t)t * (H / 32), H / 8,
+                                 xfull + xs_);
+                    }
+                    const uint8_t *gb = mat_ptr(RT, Ld, a, ci.e, 0);
+                    const uint8_t *ub = mat_ptr(RT, Ld, a, ci.e, 1);
+                    for (int s = 0; s < C::SPI; ++s) {
+                        if (it == bx && s < npre) {  // copied during the previous layer
+                            gR.next(NS_G);
+                            continue;
+                        }
+                        issue_gu(gR, gb, ub, (size_t)rt * MOE_ROWTILE + (size_t)s * C::SR);
+                    }
                 }
-            }
-        }
-        return;
-    }
-
-    // consumers: warps 0..7
-    pdl_wait();
-    const long long n_items = (long long)__ldcg(a.hdr + HDR_NCHUNKS) * R;
-    const int rho = lane / G::LPR, lr = lane % G::LPR, bb = lr >> 2, sub = lr & 3;
-    const int rs = warp * G::RPW + rho;           // row inside a sub-stage
-    const bool has_rows = warp * G::RPW < C::SR;  // H = 256: only warps 0..3 have rows
-    XSlice X[G::CP];
-    int n = 0, i = 0;
-    for (long long it = blockIdx.x; it < n_items; it += gridDim.x, ++i) {
-        const int rt = (int)(it % R);
-        const int xsl = i & 1;
-        if (!mbar_wait(xfull + xsl, (unsigned)((i >> 1) & 1))) return;
-        const uint8_t *xb = xst + (size_t)xsl * XSLOT;
-        const MoeChunk *ch = reinterpret_cast<const MoeChunk *>(xb);
-        const int np = ch->np, p0 = ch->p0;
-        const int16_t *xq = reinterpret_cast<const int16_t *>(xb + CHUNK_HDR);
-        const float *xsc = reinterpret_cast<const float *>(xb + CHUNK_HDR + (size_t)TC * H * 2);
-        for (int s = 0; s < C::SPI; ++s, ++n) {
-            const int slot = n % C::NS;
-            if (!mbar_wait(wfull + slot, (unsigned)((n / C::NS) & 1))) return;
-            const uint8_t *grow = wst + (size_t)slot * C::STB + (size_t)rs * G::ROWB;
-            const uint8_t *urow = grow + (size_t)C::SR * G::ROWB;
-            for (int j = 0; has_rows && j < np; ++j) {
-                if (np > 1 || s == 0) {  // one token: its slice stays in registers across sub-stages
-#pragma unroll
-                    for (int cp = 0; cp < G::CP; ++cp)
-                        load_slice_q4k(X[cp], xq + (size_t)j * H, xsc + (size_t)j * (H / 32),
-                                       QK * (cp * 8 + bb) + 64 * sub);
+                npre = 0;
+                if (a.stamps) pstamp(l, 11);
+                // down stages (tile it3, chunk c), tile-major: the weights depend
+                // only on the routing, so the first NS_D go out now and are in
+                // flight while the gate/up items compute; the intermediate
+                // follows after the grid barrier
+                auto issue_dw = [&](Ring &d, const ChunkInfo &ci, int it3) {
+                    if (d.used) swait(dempty + d.slot, (unsigned)(d.phase ^ 1));
+                    const uint8_t *db = mat_ptr(RT, Ld, a, ci.e, 2);
+                    if (db && !(reinterpret_cast<uintptr_t>(db) & 15)) {
+                        mbar_arrive_expect_tx(dw + d.slot, (unsigned)C::WB);
+                        bulk_g2s(dring + (size_t)d.slot * m.dslot, db + (size_t)it3 * MOE_RT3 * GI::ROWB,
+                                 (unsigned)C::WB, dw + d.slot);
+                    } else {
+                        flag_error(DEVERR_ROUTE);
+                        mbar_arrive(dw + d.slot);
+                    }
+                };
+                auto issue_da = [&](const Ring &d, const ChunkInfo &ci) {
+                    uint8_t *st = dring + (size_t)d.slot * m.dslot + C::WB;
+                    mbar_arrive_expect_tx(da + d.slot, (unsigned)(ci.np * C::ATOK));
+                    bulk_g2s(st, a.aq + (size_t)ci.p0 * I, (unsigned)(ci.np * I * 2), da + d.slot);
+                    bulk_g2s(st + (size_t)TC * I * 2, a.as + (size_t)ci.p0 * (I / 32), (unsigned)(ci.np * (I / 8)),
+                             da + d.slot);
+                };
+                const Ring d0 = dR;
+                int dpre = 0;
+                {
+                    Ring d = d0;
+                    for (int it3 = bx; it3 < NT && dpre < NS_D; it3 += G)
+                        for (int c = 0; c < nch && dpre < NS_D; ++c, ++dpre) {
+                            issue_dw(d, chunk_info(RT, c), it3);
+                            d.next(NS_D);
+                        }
                 }
-                float gs = 0.0f, us = 0.0f;
-#pragma unroll
-                for (int cp = 0; cp < G::CP; ++cp) {
-                    gs += q4k_lane_dot(grow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
-                    us += q4k_lane_dot(urow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                if (a.stamps) pstamp(l, 12);
+                if (l + 1 < a.L) issue_router(l + 1);  // consumers are past phase A
+                if (a.stamps) pstamp(l, 13);
+                // the intermediate of every CTA is complete after grid barrier (phase B)
+                const int bidx = ep ? 2 * l + 1 : 3 * l + 1;
+                wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(bidx + 1) * G, false, GRID_WAIT_NS);
+                fence_proxy_async_global();
+                if (a.stamps) pstamp(l, 14);
+                {
+                    Ring d = d0;
+                    int n = 0;
+                    for (int it3 = bx; it3 < NT; it3 += G)
+                        for (int c = 0; c < nch; ++c, ++n) {
+                            const ChunkInfo ci = chunk_info(RT, c);
+                            if (n >= dpre) issue_dw(d, ci, it3);
+                            issue_da(d, ci);
+                            d.next(NS_D);
+                        }
+                    dR = d;
                 }
-#pragma unroll
-                for (int o = G::LPR / 2; o; o >>= 1) {
-                    gs += __shfl_xor_sync(0xffffffffu, gs, o);
-                    us += __shfl_xor_sync(0xffffffffu, us, o);
-                }
-                if (lr == 0) abuf[j * MOE_ROWTILE + s * C::SR + rs] = gs / (1.0f + expf(-gs)) * us;
+                if (a.stamps) pstamp(l, 15);
+                if (l + 1 < a.L) npre = preissue_shared(l + 1);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(wempty + slot);
-        }
-        named_sync(1, 256);
-        if (lane == 0) mbar_arrive(xempty + xsl);
-        for (int j = warp; j < np; j += 8) {
-            const size_t p = (size_t)(p0 + j);
-            const int q = quant32(abuf[j * MOE_ROWTILE + lane], a.as + p * (a.I / 32) + rt, lane);
-            a.aq[p * a.I + (size_t)rt * MOE_ROWTILE + lane] = (int16_t)q;
-        }
-        named_sync(1, 256);
-    }
-}
-
-// ---------------------------------------------------------------------------
-// K3: down + weighted combine
-// ---------------------------------------------------------------------------
-template <int NB>
-struct K3Cfg {
-    using G = MGeo<BREAD_QTYPE_Q6_K, NB>;
-    static constexpr int I = QK * NB;
-    static constexpr int WS = MOE_RT3 / G::RPW;              // warp steps per stage
-    static constexpr size_t WB = (size_t)MOE_RT3 * G::ROWB;  // weight bytes per stage
-    static constexpr size_t ABY = (size_t)I * 2 + I / 8;     // one pair's intermediate + its scales
-    static constexpr size_t STB = al16(CHUNK_HDR + WB + MOE_TC * ABY);
-    static constexpr int NS0 = (int)((96 * 1024) / STB);
-    static constexpr int NS = NS0 < 2 ? 2 : (NS0 > 16 ? 16 : NS0);
-    static constexpr size_t BAR_OFF = (size_t)NS * STB + 16;
-    static constexpr size_t ACC_OFF = BAR_OFF + 2 * NS * 8;
-    __host__ __device__ static size_t smem(int T) { return ACC_OFF + (size_t)8 * T * MOE_RT3 * 4; }
-};
-
-template <int NB>
-__global__ void __launch_bounds__(288) moe_down_kernel(MoeArgs a)
-{
-    using C = K3Cfg<NB>;
-    using G = typename C::G;
-    constexpr int I = C::I;
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t *stages = smem;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
-    uint64_t *empty = full + C::NS;
-    float *accs = reinterpret_cast<float *>(smem + C::ACC_OFF);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int T = a.T;
-    if (tid == 0) {
-        for (int s = 0; s < C::NS; ++s) {
-            mbar_init(full + s, 1);
-            mbar_init(empty + s, C::WS);
-        }
-        fence_mbar_init();
-    }
-    for (int i = tid; i < 8 * T * MOE_RT3; i += blockDim.x) accs[i] = 0.0f;
-    __syncthreads();
-    const int n_items = a.H / MOE_RT3;
-    // This kernel starts once every gate/up CTA has passed its own wait on the
-    // router, so the chunk table is complete and is read before this kernel's
-    // wait -- through L2, since the previous layer's table may sit in L1.
-    const int nch = __ldcg(a.hdr + HDR_NCHUNKS);
-    const int my_items = (int)blockIdx.x < n_items ? (n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int n_stages = my_items * nch;
-
-    if (warp == 8) {  // producer: lane j feeds stage base + j of each batch of NS stages
-        if (n_stages == 0) {
-            pdl_wait();
-            pdl_launch_dependents();
-            return;
-        }
-        for (int base = 0; base < n_stages; base += C::NS) {
-            const int n = base + lane;
-            const bool act = lane < C::NS && n < n_stages;
-            const int slot = n % C::NS;
-            const MoeChunk *cp = nullptr;
-            int np = 0, p0 = 0;
-            if (act) {
-                if (n >= C::NS && !mbar_wait(empty + slot, (unsigned)(((n / C::NS) - 1) & 1))) return;
-                const int it = (int)blockIdx.x + (n / nch) * (int)gridDim.x;
-                cp = a.chunks + (n % nch);
-                const uint8_t *db =
-                    reinterpret_cast<const uint8_t *>(__ldcg(reinterpret_cast<const unsigned long long *>(&cp->down)));
-                np = __ldcg(&cp->np);
-                p0 = __ldcg(&cp->p0);
-                const bool ok = db && !(reinterpret_cast<uintptr_t>(db) & 15);
-                if (!ok) flag_error(DEVERR_ROUTE);
-                uint8_t *st = stages + (size_t)slot * C::STB;
-                mbar_arrive_expect_tx(full + slot,
-                                      (unsigned)(sizeof(MoeChunk) + (ok ? C::WB : 0) + (size_t)np * (I * 2 + I / 8)));
-                bulk_g2s(st, cp, sizeof(MoeChunk), full + slot);
-                if (ok) bulk_g2s(st + CHUNK_HDR, db + (size_t)it * MOE_RT3 * G::ROWB, (unsigned)C::WB, full + slot);
-            }
-            if (base == 0) {
-                pdl_wait();  // the intermediate comes from the gate/up kernel
-                pdl_launch_dependents();
-            }
-            if (act && np > 0) {
-                uint8_t *st = stages + (size_t)slot * C::STB;
-                bulk_g2s(st + CHUNK_HDR + C::WB, a.aq + (size_t)p0 * I, (unsigned)(np * I * 2), full + slot);
-                bulk_g2s(st + CHUNK_HDR + C::WB + (size_t)MOE_TC * I * 2, a.as + (size_t)p0 * (I / 32),
-                         (unsigned)(np * (I / 8)), full + slot);
-            }
         }
         return;
     }
 
-    pdl_wait();
-    const int rho = lane / G::LPR, lr = lane % G::LPR, bb = lr >> 2, sub = lr & 3;
-    const Q6Lane L6 = q6_lane(((rho * NB + bb) & 1) ? 2 : 0, sub & 1);
-    float *my_acc = accs + (size_t)warp * T * MOE_RT3;
-    int n = 0;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-        for (int c = 0; c < nch; ++c, ++n) {
-            const int slot = n % C::NS;
-            const uint8_t *st = stages + (size_t)slot * C::STB;
-            bool waited = false;
-            for (int ws = 0; ws < C::WS; ++ws) {
-                if (((c * C::WS + ws) & 7) != warp) continue;
-                if (!waited) {
-                    if (!mbar_wait(full + slot, (unsigned)((n / C::NS) & 1))) return;
-                    waited = true;
+    // ==================================================================== consumers
+    Ring gR, dR;
+    int nX = 0;
+    int bar = 0;
+    const bool stamp = a.stamps && tid == 0;
+    auto stamp_at = [&](int l, int k) { a.stamps[((size_t)l * G + bx) * STAMPS + k] = globaltimer(); };
+    for (int l = 0; l < a.L; ++l) {
+        const StepLayer Ld = layer_desc(a, l);
+        // ------------------------------------------------------------ phase A
+        const float *src = in_of(a, l);
+        const float *pmb = nullptr;  // layer l-1's partials in this rank's mailbox (EP)
+        if (ep && l > 0) {
+            const int s = ep_slot(a.L, l - 1);
+            if (tid == 0) wait_counter(ep_counter(a, a.ep_rank, s), ep_target(a, l - 1, epoch, NT), true, EP_WAIT_NS);
+            named_sync(BAR_CONS, ST_CONS);
+            src = in_of(a, l - 1);
+            pmb = a.ep_mb[a.ep_rank] + mb_slot_off(s, a);
+        }
+        if (stamp) stamp_at(l, 0);
+        const size_t TH = (size_t)a.ep_tmax * H;
+        auto xin = [&](size_t i) -> float {
+            float v = __ldcg(src + i);
+            if (pmb)
+                for (int r = 0; r < a.ep_world; ++r) v += __ldcv(pmb + (size_t)r * TH + i);
+            return v;
+        };
+        // (1) this CTA's share of the int16 quantisation (+ group sums of squares)
+        {
+            const int ngr = T * (H / 32);
+            for (int gi = bx * 8 + warp; gi < ngr; gi += G * 8) {
+                const float v = xin((size_t)gi * 32 + lane);
+                const float ss = warp_sum(v * v);
+                if (lane == 0) a.ssq[gi] = ss;
+                const int q = quant32(v, a.xs + gi, lane);
+                a.xq[(size_t)gi * 32 + lane] = (int16_t)q;
+            }
+        }
+        // (2) EP: the owner of each column tile materialises this layer's input
+        if (pmb) {
+            float *dst = const_cast<float *>(in_of(a, l));
+            for (int it3 = bx; it3 < NT; it3 += G)
+                for (int i = tid; i < T * MOE_RT3; i += ST_CONS) {
+                    const size_t o = (size_t)(i / MOE_RT3) * H + (size_t)it3 * MOE_RT3 + i % MOE_RT3;
+                    dst[o] = xin(o);
                 }
-                const MoeChunk *ch = reinterpret_cast<const MoeChunk *>(st);
-                const int np = ch->np;
-                const uint8_t *rowp = st + CHUNK_HDR + (size_t)ws * G::STEPB + (size_t)rho * G::ROWB;
-                const int16_t *aqs = reinterpret_cast<const int16_t *>(st + CHUNK_HDR + C::WB);
-                const float *ass = reinterpret_cast<const float *>(st + CHUNK_HDR + C::WB + (size_t)MOE_TC * I * 2);
-                for (int j = 0; j < np; ++j) {
-                    const int t = ch->tok[j];
-                    const float wgt = ch->w[j];
-                    float v = 0.0f;
-#pragma unroll
-                    for (int cp = 0; cp < G::CP; ++cp) {
-                        XSlice X;
-                        load_slice_q6k(X, aqs + (size_t)j * I, ass + (size_t)j * (I / 32),
-                                       QK * (cp * 8 + bb) + 128 * (sub >> 1), sub & 1);
-                        v += q6k_lane_dot(rowp + (size_t)(cp * 8 + bb) * Q6K_BYTES, sub >> 1, sub & 1, L6, X);
+        }
+        // (3) router rows of this CTA (row E = fp16 shared-gate vector)
+        swait(rbar, (unsigned)(l & 1));
+        {
+            const int rl = warp / m.WPR, qt = warp % m.WPR;
+            const int row = bx * m.RR + rl;
+            const int nrows = E + (Ld.w_sg ? 1 : 0);
+            const int seg = H / m.WPR, c0 = qt * seg;
+            if (row < nrows) {
+                const float *wr = rbuf + (size_t)rl * H;
+                const __half *wh = reinterpret_cast<const __half *>(wr);
+                for (int t = 0; t < T; ++t) {
+                    float s = 0.0f;
+#pragma unroll 4
+                    for (int c = c0 + lane; c < c0 + seg; c += 32) {
+                        const float w = row < E ? wr[c] : __half2float(wh[c]);
+                        s = fmaf(w, xin((size_t)t * H + c), s);
                     }
-#pragma unroll
-                    for (int o = G::LPR / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                    if (lr == 0) my_acc[t * MOE_RT3 + ws * G::RPW + rho] += wgt * v;
+                    s = warp_sum(s);
+                    if (lane == 0) part[(rl * m.WPR + qt) * T + t] = s;
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(empty + slot);
+            }
+            named_sync(BAR_CONS, ST_CONS);
+            for (int i = tid; i < m.RR * T; i += ST_CONS) {
+                const int r_l = i / T, t = i % T, rr = bx * m.RR + r_l;
+                if (rr < nrows) {
+                    float v = 0.0f;
+                    for (int q = 0; q < m.WPR; ++q) v += part[(r_l * m.WPR + q) * T + t];
+                    if (rr < E)
+                        a.logits[(size_t)t * E + rr] = v;
+                    else
+                        a.score[t] = v;
+                }
             }
         }
-        named_sync(1, 256);
-        for (int i = tid; i < T * MOE_RT3; i += 256) {
-            const int t = i / MOE_RT3, r = i % MOE_RT3;
-            float s = 0.0f;
-#pragma unroll
-            for (int w = 0; w < 8; ++w) {
-                s += accs[(size_t)w * T * MOE_RT3 + i];
-                accs[(size_t)w * T * MOE_RT3 + i] = 0.0f;
-            }
-            const size_t oi = (size_t)t * a.H + (size_t)it * MOE_RT3 + r;
-            if (a.ep_world > 1) {
-                // this rank's partial -> slot [ep_slot][ep_rank] of every rank's mailbox (NVLink stores)
-                const size_t off = MoeMailbox::data_off(a.ep_slot, a.ep_rank, a.ep_world, a.ep_tmax, a.H) / 4 + oi;
-                for (int p = 0; p < a.ep_world; ++p) a.ep_mb[p][off] = s;
-            } else {
-                a.out[oi] = a.out[oi] + s;
-            }
-        }
-        named_sync(1, 256);
-    }
-    if (a.ep_world > 1) {
-        // one arrival per CTA at every rank, after all of this CTA's stores
-        __threadfence_system();
-        named_sync(1, 256);
-        if (tid == 0) {
-            const MoeMailbox L = MoeMailbox::make(a.ep_world, a.ep_tmax, a.H);
-            for (int p = 0; p < a.ep_world; ++p) {
-                unsigned *f = reinterpret_cast<unsigned *>(reinterpret_cast<uint8_t *>(a.ep_mb[p]) + L.flag_off) +
-                              a.ep_slot * 8 + a.ep_rank;
-                atomicAdd_system(f, 1u);
-            }
-        }
-    }
-}
+        if (stamp) stamp_at(l, 1);
+        grid_barrier(a, bar++, tid);
+        if (stamp) stamp_at(l, 2);
 
-// Expert-parallel combine (one per layer, after the down kernel on every
-// rank): wait, bounded, until every rank's down-kernel CTAs have arrived in
-// this rank's mailbox slot, then h += sum over ranks (rank order, so every
-// rank gets the same bits); the last CTA re-arms the slot's counters.
-__global__ void __launch_bounds__(256) ep_combine_kernel(float *h, MoeArgs a, int n_signals)
-{
-    pdl_wait();
-    pdl_launch_dependents();
-    uint8_t *own = reinterpret_cast<uint8_t *>(a.ep_mb[a.ep_rank]);
-    const MoeMailbox L = MoeMailbox::make(a.ep_world, a.ep_tmax, a.H);
-    volatile unsigned *flags = reinterpret_cast<volatile unsigned *>(own + L.flag_off) + a.ep_slot * 8;
-    __shared__ int s_ok;
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        for (int r = 0; r < a.ep_world && ok; ++r) {
-            long long i = 0;
-            while (flags[r] < (unsigned)n_signals) {
-                if (++i > SPIN_LIMIT) {
-                    ok = 0;
-                    flag_error(DEVERR_TIMEOUT);
-                    break;
+        // ------------------------------------------------------------ phase B
+        if (E <= 256)
+            route_tables<8>(a, Ld, RT, l, bx == 0);
+        else
+            route_tables<MOE_EMAX / 32>(a, Ld, RT, l, bx == 0);
+        if (stamp) stamp_at(l, 3);
+        named_sync(BAR_ALL, ST_THREADS);
+        if (a.route_only) break;
+        const int nch = RT.scal[1];
+        {
+            const int rho = lane / GH::LPR, lr = lane % GH::LPR, bb = lr >> 2, sub = lr & 3;
+            const int rs = warp * GH::RPW + rho;            // row inside a sub-stage
+            const bool has_rows = warp * GH::RPW < C::SR;   // H = 256: only warps 0..3 have rows
+            XSlice X[GH::CP];
+            for (int it = bx; it < nch * R; it += G, ++nX) {
+                const int c = it / R, rt = it % R;  // R: a power of two
+                const ChunkInfo ci = chunk_info(RT, c);
+                const int xs_ = nX & 1;
+                swait(xfull + xs_, (unsigned)((nX >> 1) & 1));
+                if (stamp && it == bx) stamp_at(l, 4);
+                const uint8_t *xb = xsl + (size_t)xs_ * m.xslot;
+                const int16_t *xq = reinterpret_cast<const int16_t *>(xb);
+                const float *xsc = reinterpret_cast<const float *>(xb + (size_t)TC * H * 2);
+                for (int s = 0; s < C::SPI; ++s, gR.next(NS_G)) {
+                    const int slot = gR.slot;
+                    swait(gfull + slot, (unsigned)gR.phase);
+                    const uint8_t *grow = gring + (size_t)slot * C::STB + (size_t)rs * GH::ROWB;
+                    const uint8_t *urow = grow + (size_t)C::SR * GH::ROWB;
+                    for (int j = 0; has_rows && j < ci.np; ++j) {
+                        if (ci.np > 1 || s == 0) {  // one token: its slice stays in registers across sub-stages
+                            const int t = RT.ptok[ci.p0 + j];
+                            const float rsc = norm ? RT.rinv[t] : 1.0f;
+#pragma unroll
+                            for (int cp = 0; cp < GH::CP; ++cp)
+                                load_slice_q4k(X[cp], xq + (size_t)j * H, xsc + (size_t)j * (H / 32),
+                                               QK * (cp * 8 + bb) + 64 * sub, rsc);
+                        }
+                        float gs = 0.0f, us = 0.0f;
+#pragma unroll
+                        for (int cp = 0; cp < GH::CP; ++cp) {
+                            gs += q4k_lane_dot(grow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                            us += q4k_lane_dot(urow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                        }
+#pragma unroll
+                        for (int o = GH::LPR / 2; o; o >>= 1) {
+                            gs += __shfl_xor_sync(0xffffffffu, gs, o);
+                            us += __shfl_xor_sync(0xffffffffu, us, o);
+                        }
+                        if (lr == 0) abuf[j * MOE_ROWTILE + s * C::SR + rs] = gs / (1.0f + expf(-gs)) * us;
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(gempty + slot);
                 }
-                if (i > 64) __nanosleep(128);
+                named_sync(BAR_CONS, ST_CONS);
+                if (lane == 0) mbar_arrive(xempty + xs_);
+                for (int j = warp; j < ci.np; j += 8) {
+                    const size_t p = (size_t)(ci.p0 + j);
+                    const int q = quant32(abuf[j * MOE_ROWTILE + lane], a.as + p * (I / 32) + rt, lane);
+                    a.aq[p * I + (size_t)rt * MOE_ROWTILE + lane] = (int16_t)q;
+                }
+                named_sync(BAR_CONS, ST_CONS);
             }
         }
-        __threadfence_system();
-        s_ok = ok;
-    }
-    __syncthreads();
-    if (s_ok) {
-        const float *mb = reinterpret_cast<const float *>(own);
-        const size_t n = (size_t)a.T * a.H;
-        for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-            float v = h[i];
-            for (int r = 0; r < a.ep_world; ++r)
-                v += __ldcv(mb + MoeMailbox::data_off(a.ep_slot, r, a.ep_world, a.ep_tmax, a.H) / 4 + i);
-            h[i] = v;
+        if (stamp) stamp_at(l, 5);
+        grid_barrier(a, bar++, tid);
+        if (stamp) stamp_at(l, 6);
+
+        // ------------------------------------------------------------ phase C
+        {
+            float *out = out_of(a, l);
+            const float *res = a.res_is_out ? out : in_of(a, l);
+            const int slot_l = ep_slot(a.L, l);
+            const int rho = lane / GI::LPR, lr = lane % GI::LPR, bb = lr >> 2, sub = lr & 3;
+            const Q6Lane L6 = q6_lane(((rho * NBI + bb) & 1) ? 2 : 0, sub & 1);
+            float *my_acc = acc + (size_t)warp * T * MOE_RT3;
+            for (int it3 = bx; it3 < NT; it3 += G) {
+                for (int c = 0; c < nch; ++c, dR.next(NS_D)) {
+                    const int slot = dR.slot;
+                    const unsigned par = (unsigned)dR.phase;
+                    const uint8_t *st = dring + (size_t)slot * m.dslot;
+                    bool waited = false;
+                    ChunkInfo ci{0, 0, 0};
+                    for (int ws = 0; ws < C::WS; ++ws) {
+                        if (((c * C::WS + ws) & 7) != warp) continue;
+                        if (!waited) {
+                            swait(dw + slot, par);
+                            swait(da + slot, par);
+                            if (stamp && c == 0 && it3 == bx) stamp_at(l, 7);
+                            ci = chunk_info(RT, c);
+                            waited = true;
+                        }
+                        const uint8_t *rowp = st + (size_t)ws * GI::STEPB + (size_t)rho * GI::ROWB;
+                        const int16_t *aqs = reinterpret_cast<const int16_t *>(st + C::WB);
+                        const float *ass = reinterpret_cast<const float *>(st + C::WB + (size_t)TC * I * 2);
+                        for (int j = 0; j < ci.np; ++j) {
+                            const int t = RT.ptok[ci.p0 + j];
+                            const float wgt = RT.pw[ci.p0 + j];
+                            float v = 0.0f;
+#pragma unroll
+                            for (int cp = 0; cp < GI::CP; ++cp) {
+                                XSlice X;
+                                load_slice_q6k(X, aqs + (size_t)j * I, ass + (size_t)j * (I / 32),
+                                               QK * (cp * 8 + bb) + 128 * (sub >> 1), sub & 1);
+                                v += q6k_lane_dot(rowp + (size_t)(cp * 8 + bb) * Q6K_BYTES, sub >> 1, sub & 1, L6, X);
+                            }
+#pragma unroll
+                            for (int o = GI::LPR / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                            if (lr == 0) my_acc[t * MOE_RT3 + ws * GI::RPW + rho] += wgt * v;
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(dempty + slot);
+                    }
+                }
+                named_sync(BAR_CONS, ST_CONS);
+                for (int i = tid; i < T * MOE_RT3; i += ST_CONS) {
+                    const int t = i / MOE_RT3, r = i % MOE_RT3;
+                    float s = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < 8; ++w) {
+                        s += acc[(size_t)w * T * MOE_RT3 + i];
+                        acc[(size_t)w * T * MOE_RT3 + i] = 0.0f;
+                    }
+                    const size_t oi = (size_t)t * H + (size_t)it3 * MOE_RT3 + r;
+                    if (ep) {
+                        // this rank's partial -> slot [slot_l][ep_rank] of every rank's mailbox (NVLink stores)
+                        const size_t off = mb_slot_off(slot_l, a) + (size_t)a.ep_rank * TH + oi;
+                        for (int p = 0; p < a.ep_world; ++p) a.ep_mb[p][off] = s;
+                    } else {
+                        out[oi] = __ldcg(res + oi) + s;
+                    }
+                }
+                if (ep) {
+                    __threadfence_system();
+                    named_sync(BAR_CONS, ST_CONS);
+                    if (tid == 0)
+                        for (int p = 0; p < a.ep_world; ++p) atomicAdd_system(ep_counter(a, p, slot_l), 1ull);
+                }
+                named_sync(BAR_CONS, ST_CONS);
+            }
         }
+        if (stamp) stamp_at(l, 8);
+        if (!ep) grid_barrier(a, bar++, tid);
+        if (stamp) stamp_at(l, 9);
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned *ticket = reinterpret_cast<unsigned *>(own + L.ticket_off) + a.ep_slot;
+
+    // EP: the last layer's partials -> output columns owned by this CTA
+    if (ep && !a.route_only) {
+        const int s = ep_slot(a.L, a.L - 1);
+        if (tid == 0) wait_counter(ep_counter(a, a.ep_rank, s), ep_target(a, a.L - 1, epoch, NT), true, EP_WAIT_NS);
+        named_sync(BAR_CONS, ST_CONS);
+        const float *src = in_of(a, a.L - 1);
+        const float *pmb = a.ep_mb[a.ep_rank] + mb_slot_off(s, a);
+        const size_t TH = (size_t)a.ep_tmax * H;
+        for (int it3 = bx; it3 < NT; it3 += G)
+            for (int i = tid; i < T * MOE_RT3; i += ST_CONS) {
+                const size_t o = (size_t)(i / MOE_RT3) * H + (size_t)it3 * MOE_RT3 + i % MOE_RT3;
+                float v = __ldcg(src + o);
+                for (int r = 0; r < a.ep_world; ++r) v += __ldcv(pmb + (size_t)r * TH + o);
+                a.y[o] = v;
+            }
+    }
+
+    // exit ticket: the last CTA re-arms the barrier counter and advances the epoch
+    named_sync(BAR_CONS, ST_CONS);
+    if (tid == 0) {
         __threadfence();
-        if (atomicAdd(ticket, 1u) == gridDim.x - 1) {
-            for (int r = 0; r < a.ep_world; ++r) flags[r] = 0;
-            *ticket = 0;
-            __threadfence_system();
+        const unsigned long long prev = atomicAdd(a.ctrl + CTRL_EXIT, 1ull);
+        if (prev == (unsigned long long)G - 1) {
+            a.ctrl[CTRL_GRID] = 0;
+            a.ctrl[CTRL_EXIT] = 0;
+            a.ctrl[CTRL_EPOCH] = epoch + 1;
+            __threadfence();
         }
     }
 }
@@ -800,40 +1011,174 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(float *h, MoeArgs a, in
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                              Args &&...args)
+template <int NBH, int NBI>
+static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G)
 {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    using C = SCfg<NBH, NBI>;
+    size_t o = 0;
+    auto take = [&](size_t n, size_t al) {
+        o = (o + al - 1) / al * al;
+        const size_t at = o;
+        o += n;
+        return (uint32_t)at;
+    };
+    const int need = (E + 1 + G - 1) / G;
+    int rr = 1;
+    while (rr < need) rr <<= 1;
+    if (rr > 8) return -1;
+    m.RR = rr;
+    m.WPR = 8 / rr;
+    m.rbuf = take((size_t)rr * C::H * 4, 128);
+    m.part = take((size_t)8 * T * 4, 16);
+    const int GM = (EL < T * K ? EL : T * K) + 1, PM = T * (K + 1);
+    m.r_idx = take((size_t)T * K * 4, 16);
+    m.r_w = take((size_t)T * K * 4, 16);
+    m.r_rinv = take((size_t)T * 4, 16);
+    m.r_sgw = take((size_t)T * 4, 16);
+    m.r_cnt = take((size_t)(EL > 0 ? EL : 1) * 4, 16);
+    m.r_run = take((size_t)(EL > 0 ? EL : 1) * 4, 16);
+    m.r_off = take((size_t)(EL > 0 ? EL : 1) * 4, 16);
+    m.r_gexp = take((size_t)GM * 4, 16);
+    m.r_goff = take((size_t)GM * 4, 16);
+    m.r_gcnt = take((size_t)GM * 4, 16);
+    m.r_gcpre = take((size_t)(GM + 1) * 4, 16);
+    m.r_ptok = take((size_t)PM * 4, 16);
+    m.r_pw = take((size_t)PM * 4, 16);
+    m.r_scal = take(16, 16);
+    m.r_ptr = take((size_t)(EL > 0 ? EL : 1) * 3 * sizeof(void *), 16);
+    m.r_chunk = take((size_t)(GM + (PM + MOE_TC - 1) / MOE_TC) * sizeof(int4), 16);
+    const int TC = T < MOE_TC ? T : MOE_TC;
+    m.xslot = (uint32_t)al16((size_t)TC * C::XTOK);
+    m.xsl = take(2 * (size_t)m.xslot, 128);
+    int nsg = 4;
+    while (nsg > 2 && (size_t)nsg * C::STB > 80 * 1024) --nsg;
+    if (T > MOE_TC) nsg = 2;
+    m.NS_G = nsg;
+    m.gring = take((size_t)nsg * C::STB, 128);
+    m.abuf = take((size_t)TC * MOE_ROWTILE * 4, 16);
+    m.acc = take((size_t)8 * T * MOE_RT3 * 4, 16);
+    m.dslot = (uint32_t)al16((size_t)C::WB + (size_t)TC * C::ATOK);
+    const size_t bars_max = (size_t)(1 + 2 * nsg + 4 + 3 * 16) * 8 + 8;
+    const size_t d0 = (o + 127) / 128 * 128;
+    const size_t avail = SMEM_LIMIT > d0 + bars_max ? SMEM_LIMIT - d0 - bars_max : 0;
+    int nsd = (int)(avail / m.dslot);
+    if (nsd > 16) nsd = 16;
+    if (nsd < 2) return -1;
+    m.NS_D = nsd;
+    m.dring = take((size_t)nsd * m.dslot, 128);
+    m.bars = take((size_t)(1 + 2 * nsg + 4 + 3 * nsd) * 8, 8);
+    m.total = (uint32_t)o;
+    return o <= SMEM_LIMIT ? 0 : -1;
 }
 
-void moe_bind_workspace(MoeArgs &a, void *ws, const MoeWs &L)
+constexpr int MAX_DEVICES = 64;
+
+template <int NBH, int NBI>
+static int setup_nb()
+{
+    static std::mutex mu;
+    static bool done[MAX_DEVICES] = {};
+    int dev = 0;
+    BREAD_CUDA(cudaGetDevice(&dev), "moe step: cudaGetDevice");
+    if (dev < 0 || dev >= MAX_DEVICES) return set_error(BREAD_ERR_STATE, "moe step: device %d", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+        BREAD_CUDA(cudaFuncSetAttribute(moe_step_kernel<NBH, NBI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)SMEM_LIMIT),
+                   "moe step: shared-memory attribute");
+        int n = 0;
+        BREAD_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, moe_step_kernel<NBH, NBI>, ST_THREADS, SMEM_LIMIT),
+                   "moe step: occupancy");
+        if (n < 1) return set_error(BREAD_ERR_CUDA, "moe step: kernel does not fit on an SM");
+        done[dev] = true;
+    }
+    return BREAD_OK;
+}
+
+template <int NBH, int NBI>
+static int launch_nb(StepArgs &a, cudaStream_t s)
+{
+    BREAD_TRY(setup_nb<NBH, NBI>());
+    const int G = sm_count();
+    if (step_layout<NBH, NBI>(a.sm, a.T, a.top_k, a.E, a.hi - a.lo, G))
+        return set_error(BREAD_ERR_ARG, "moe step: T=%d H=%d I=%d does not fit in shared memory", a.T, a.H, a.I);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(ST_THREADS);
+    cfg.dynamicSmemBytes = a.sm.total;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI>, a), "moe step launch");
+    return BREAD_OK;
+}
+
+template <int NBH>
+static int launch_h(StepArgs &a, cudaStream_t s, int nbi)
+{
+    switch (nbi) {
+    case 1: return launch_nb<NBH, 1>(a, s);
+    case 2: return launch_nb<NBH, 2>(a, s);
+    case 4: return launch_nb<NBH, 4>(a, s);
+    case 8: return launch_nb<NBH, 8>(a, s);
+    default: return set_error(BREAD_ERR_ARG, "moe: unsupported I=%d", a.I);
+    }
+}
+
+int step_launch(StepArgs &a, cudaStream_t s)
+{
+    const int nbi = a.route_only ? 1 : a.I / QK;
+    switch (a.H / QK) {
+    case 1: return launch_h<1>(a, s, nbi);
+    case 2: return launch_h<2>(a, s, nbi);
+    case 4: return launch_h<4>(a, s, nbi);
+    case 8: return launch_h<8>(a, s, nbi);
+    case 16: return launch_h<16>(a, s, nbi);
+    default: return set_error(BREAD_ERR_ARG, "moe: unsupported H=%d", a.H);
+    }
+}
+
+template <int NBH>
+static int setup_h(int nbi)
+{
+    switch (nbi) {
+    case 1: return setup_nb<NBH, 1>();
+    case 2: return setup_nb<NBH, 2>();
+    case 4: return setup_nb<NBH, 4>();
+    case 8: return setup_nb<NBH, 8>();
+    default: return set_error(BREAD_ERR_ARG, "moe: unsupported I=%d", nbi * QK);
+    }
+}
+
+int step_setup(int H, int I)
+{
+    const int nbi = I > 0 ? I / QK : 1;
+    switch (H / QK) {
+    case 1: return setup_h<1>(nbi);
+    case 2: return setup_h<2>(nbi);
+    case 4: return setup_h<4>(nbi);
+    case 8: return setup_h<8>(nbi);
+    case 16: return setup_h<16>(nbi);
+    default: return set_error(BREAD_ERR_ARG, "moe: unsupported H=%d", H);
+    }
+}
+
+void step_bind_workspace(StepArgs &a, void *ws, const StepWs &L)
 {
     uint8_t *b = static_cast<uint8_t *>(ws);
-    a.hdr = reinterpret_cast<int *>(b + L.hdr);
+    a.ctrl = reinterpret_cast<unsigned long long *>(b + L.ctrl);
     a.logits = reinterpret_cast<float *>(b + L.logits);
-    a.ssq = reinterpret_cast<float *>(b + L.ssq);
     a.score = reinterpret_cast<float *>(b + L.score);
-    a.ridx = reinterpret_cast<int *>(b + L.ridx);
-    a.rw = reinterpret_cast<float *>(b + L.rw);
-    a.sgw = reinterpret_cast<float *>(b + L.sgw);
+    a.ssq = reinterpret_cast<float *>(b + L.ssq);
     a.xq = reinterpret_cast<int16_t *>(b + L.xq);
     a.xs = reinterpret_cast<float *>(b + L.xs);
-    a.p_token = reinterpret_cast<int *>(b + L.p_token);
-    a.p_w = reinterpret_cast<float *>(b + L.p_w);
-    a.chunks = reinterpret_cast<MoeChunk *>(b + L.chunks);
     a.aq = reinterpret_cast<int16_t *>(b + L.aq);
     a.as = reinterpret_cast<float *>(b + L.as);
+    a.buf[0] = L.buf0 ? reinterpret_cast<float *>(b + L.buf0) : nullptr;
+    a.buf[1] = L.buf1 ? reinterpret_cast<float *>(b + L.buf1) : nullptr;
 }
 
 static bool nb_ok_h(int nb) { return nb == 1 || nb == 2 || nb == 4 || nb == 8 || nb == 16; }
@@ -852,128 +1197,6 @@ int moe_check_shapes(int T, int H, int I, int E, int top_k, bool need_experts)
     return BREAD_OK;
 }
 
-int moe_launch_route(const MoeArgs &a, cudaStream_t s)
-{
-    const dim3 grid((a.E + (a.w_sg ? 1 : 0) + K1_ROWS - 1) / K1_ROWS, (a.T + K1_TG - 1) / K1_TG);
-    BREAD_CUDA(launch_pdl(moe_route_kernel, grid, dim3(256), 0, s, a), "moe route launch");
-    return BREAD_OK;
-}
-
-template <int NB>
-static int setup_gateup_nb()
-{
-    static bool done = false;
-    if (!done) {
-        BREAD_CUDA(cudaFuncSetAttribute(moe_gateup_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)K2Cfg<NB>::smem(MOE_TMAX)),
-                   "moe gate/up smem attribute");
-        done = true;
-    }
-    return BREAD_OK;
-}
-
-template <int NB>
-static int launch_gateup_nb(const MoeArgs &a, cudaStream_t s)
-{
-    BREAD_TRY(setup_gateup_nb<NB>());
-    BREAD_CUDA(launch_pdl(moe_gateup_kernel<NB>, dim3(sm_count()), dim3(288), K2Cfg<NB>::smem(a.T), s, a),
-               "moe gate/up launch");
-    return BREAD_OK;
-}
-
-int moe_launch_gateup(const MoeArgs &a, cudaStream_t s)
-{
-    switch (a.H / 256) {
-    case 1: return launch_gateup_nb<1>(a, s);
-    case 2: return launch_gateup_nb<2>(a, s);
-    case 4: return launch_gateup_nb<4>(a, s);
-    case 8: return launch_gateup_nb<8>(a, s);
-    case 16: return launch_gateup_nb<16>(a, s);
-    default: return set_error(BREAD_ERR_ARG, "moe: unsupported H=%d", a.H);
-    }
-}
-
-// Grid of the down kernel (also the number of arrivals each rank's combine
-// waits for).  The smem attribute and occupancy are set up once.
-template <int NB>
-static int down_grid_nb(const MoeArgs &a)
-{
-    using C = K3Cfg<NB>;
-    static int per_sm = 0;
-    if (!per_sm) {
-        if (cudaFuncSetAttribute(moe_down_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)C::smem(MOE_TMAX)) != cudaSuccess)
-            return -1;
-        int n = 1;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, moe_down_kernel<NB>, 288, C::smem(1)) != cudaSuccess)
-            return -1;
-        per_sm = n < 1 ? 1 : n;
-    }
-    const int items = a.H / MOE_RT3;
-    const int cap = sm_count() * (a.T <= 8 ? per_sm : 1);
-    return items < cap ? items : cap;
-}
-
-template <int NB>
-static int launch_down_nb(const MoeArgs &a, cudaStream_t s)
-{
-    const int grid = down_grid_nb<NB>(a);
-    if (grid < 1) return set_error(BREAD_ERR_CUDA, "moe down: kernel set-up failed");
-    BREAD_CUDA(launch_pdl(moe_down_kernel<NB>, dim3(grid), dim3(288), K3Cfg<NB>::smem(a.T), s, a), "moe down launch");
-    return BREAD_OK;
-}
-
-int moe_down_grid(const MoeArgs &a)
-{
-    switch (a.I / 256) {
-    case 1: return down_grid_nb<1>(a);
-    case 2: return down_grid_nb<2>(a);
-    case 4: return down_grid_nb<4>(a);
-    default: return down_grid_nb<8>(a);
-    }
-}
-
-int moe_launch_down(const MoeArgs &a, cudaStream_t s)
-{
-    switch (a.I / 256) {
-    case 1: return launch_down_nb<1>(a, s);
-    case 2: return launch_down_nb<2>(a, s);
-    case 4: return launch_down_nb<4>(a, s);
-    case 8: return launch_down_nb<8>(a, s);
-    default: return set_error(BREAD_ERR_ARG, "moe: unsupported I=%d", a.I);
-    }
-}
-
-// One-time kernel attribute set-up for these shapes (before any graph capture).
-int moe_setup_kernels(int H, int I)
-{
-    int st = BREAD_OK;
-    switch (H / 256) {
-    case 1: st = setup_gateup_nb<1>(); break;
-    case 2: st = setup_gateup_nb<2>(); break;
-    case 4: st = setup_gateup_nb<4>(); break;
-    case 8: st = setup_gateup_nb<8>(); break;
-    case 16: st = setup_gateup_nb<16>(); break;
-    default: return set_error(BREAD_ERR_ARG, "moe: unsupported H=%d", H);
-    }
-    if (st) return st;
-    MoeArgs a{};
-    a.H = H;
-    a.I = I;
-    a.T = 1;
-    return moe_down_grid(a) > 0 ? BREAD_OK : set_error(BREAD_ERR_CUDA, "moe down: kernel set-up failed");
-}
-
-int moe_launch_combine(const MoeArgs &a, float *h, cudaStream_t s)
-{
-    const int n = a.T * a.H;
-    int grid = (n + 255) / 256;
-    if (grid > sm_count()) grid = sm_count();
-    BREAD_CUDA(launch_pdl(ep_combine_kernel, dim3(grid), dim3(256), 0, s, h, a, moe_down_grid(a)),
-               "ep combine launch");
-    return BREAD_OK;
-}
-
 }  // namespace bread
 
 using namespace bread;
@@ -981,25 +1204,26 @@ using namespace bread;
 extern "C" size_t bread_moe_workspace_bytes(int T, int H, int I, int E, int top_k)
 {
     if (T < 1 || H < 32 || E < 1 || top_k < 1) return 0;
-    return MoeWs::make(T, H, I, E, top_k).total;
+    return StepWs::make(T, H, I, E, top_k, false).total;
 }
 
-static int moe_prepare(MoeArgs &a, const float *x, const float *W_r, const void *w_sg, int T, int H, int I, int E,
+// One MoE block (L = 1): shared argument checks of the route / FFN entries.
+static int moe_prepare(StepArgs &a, const float *x, const float *W_r, const void *w_sg, int T, int H, int I, int E,
                        int top_k, void *workspace, size_t workspace_bytes, bool need_experts)
 {
     BREAD_TRY(moe_check_shapes(T, H, I, E, top_k, need_experts));
     if (!x || !W_r) return set_error(BREAD_ERR_ARG, "moe: NULL x or W_r");
-    const MoeWs L = MoeWs::make(T, H, need_experts ? I : 0, E, top_k);
+    const StepWs L = StepWs::make(T, H, need_experts ? I : 0, E, top_k, false);
     if (!workspace || workspace_bytes < L.total)
         return set_error(BREAD_ERR_WORKSPACE, "moe: workspace %zu bytes, need %zu", workspace_bytes, L.total);
     if (reinterpret_cast<uintptr_t>(workspace) & 255)
         return set_error(BREAD_ERR_ALIGN, "moe: workspace not 256-byte aligned");
-    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(W_r)) & 7)
-        return set_error(BREAD_ERR_ALIGN, "moe: x / W_r not 8-byte aligned");
-    if (reinterpret_cast<uintptr_t>(w_sg) & 3) return set_error(BREAD_ERR_ALIGN, "moe: w_sg not 4-byte aligned");
-    a = MoeArgs{};
-    a.W_r = W_r;
-    a.w_sg = static_cast<const __half *>(w_sg);
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(W_r) | reinterpret_cast<uintptr_t>(w_sg)) & 15)
+        return set_error(BREAD_ERR_ALIGN, "moe: x, W_r and w_sg must be 16-byte aligned");
+    a = StepArgs{};
+    a.l0.W_r = W_r;
+    a.l0.w_sg = static_cast<const __half *>(w_sg);
+    a.L = 1;
     a.T = T;
     a.H = H;
     a.I = I;
@@ -1009,7 +1233,9 @@ static int moe_prepare(MoeArgs &a, const float *x, const float *W_r, const void 
     a.hi = E;
     a.norm_eps = -1.0f;
     a.x = x;
-    moe_bind_workspace(a, workspace, L);
+    a.ep_world = 1;
+    a.ep_tmax = T;
+    step_bind_workspace(a, workspace, L);
     return BREAD_OK;
 }
 
@@ -1017,15 +1243,15 @@ extern "C" int bread_moe_route(const float *x, const float *W_r, const void *w_s
                                int *idx, float *w, float *sg_weight, void *workspace, size_t workspace_bytes,
                                cudaStream_t stream)
 {
-    MoeArgs a;
+    StepArgs a;
     BREAD_TRY(moe_prepare(a, x, W_r, w_sg, T, H, 0, E, top_k, workspace, workspace_bytes, false));
     if (!idx || !w) return set_error(BREAD_ERR_ARG, "moe_route: NULL idx or w");
+    a.route_only = 1;
     a.idx_out = idx;
     a.w_out = w;
     a.sg_out = sg_weight;
-    a.shared_here = 0;
-    BREAD_CUDA(cudaMemsetAsync(a.hdr, 0, 64, stream), "moe_route: reset ticket");
-    return moe_launch_route(a, stream);
+    BREAD_CUDA(cudaMemsetAsync(a.ctrl, 0, CTRL_BYTES, stream), "moe_route: reset control words");
+    return step_launch(a, stream);
 }
 
 extern "C" int bread_moe_ffn(const void *const *gate_ptrs, const void *const *up_ptrs, const void *const *down_ptrs,
@@ -1034,28 +1260,26 @@ extern "C" int bread_moe_ffn(const void *const *gate_ptrs, const void *const *up
                              int *idx_out, float *w_out, float *sg_out, void *workspace, size_t workspace_bytes,
                              cudaStream_t stream)
 {
-    MoeArgs a;
+    StepArgs a;
     BREAD_TRY(moe_prepare(a, x, W_r, w_sg, T, H, I, E, top_k, workspace, workspace_bytes, true));
-    if (!gate_ptrs || !up_ptrs || !down_ptrs || !out) return set_error(BREAD_ERR_ARG, "moe_ffn: NULL pointer table or out");
+    if (!gate_ptrs || !up_ptrs || !down_ptrs || !out)
+        return set_error(BREAD_ERR_ARG, "moe_ffn: NULL pointer table or out");
     const int nsh = (sh_gate != nullptr) + (sh_up != nullptr) + (sh_down != nullptr);
     if (nsh != 0 && nsh != 3) return set_error(BREAD_ERR_ARG, "moe_ffn: give all three shared-expert matrices or none");
     if (nsh == 3 && ((reinterpret_cast<uintptr_t>(sh_gate) | reinterpret_cast<uintptr_t>(sh_up) |
                       reinterpret_cast<uintptr_t>(sh_down)) & 15))
         return set_error(BREAD_ERR_ALIGN, "moe_ffn: shared-expert matrices must be 16-byte aligned");
-    BREAD_TRY(moe_setup_kernels(H, I));
-    a.gate = reinterpret_cast<const uint8_t *const *>(gate_ptrs);
-    a.up = reinterpret_cast<const uint8_t *const *>(up_ptrs);
-    a.down = reinterpret_cast<const uint8_t *const *>(down_ptrs);
-    a.sh_gate = static_cast<const uint8_t *>(sh_gate);
-    a.sh_up = static_cast<const uint8_t *>(sh_up);
-    a.sh_down = static_cast<const uint8_t *>(sh_down);
-    a.shared_here = nsh == 3;
-    a.out = out;
+    a.l0.gate = reinterpret_cast<const uint8_t *const *>(gate_ptrs);
+    a.l0.up = reinterpret_cast<const uint8_t *const *>(up_ptrs);
+    a.l0.down = reinterpret_cast<const uint8_t *const *>(down_ptrs);
+    a.l0.sh_gate = static_cast<const uint8_t *>(sh_gate);
+    a.l0.sh_up = static_cast<const uint8_t *>(sh_up);
+    a.l0.sh_down = static_cast<const uint8_t *>(sh_down);
+    a.res_is_out = 1;
+    a.y = out;
     a.idx_out = idx_out;
     a.w_out = w_out;
     a.sg_out = sg_out;
-    BREAD_CUDA(cudaMemsetAsync(a.hdr, 0, 64, stream), "moe_ffn: reset ticket");
-    BREAD_TRY(moe_launch_route(a, stream));
-    BREAD_TRY(moe_launch_gateup(a, stream));
-    return moe_launch_down(a, stream);
+    BREAD_CUDA(cudaMemsetAsync(a.ctrl, 0, CTRL_BYTES, stream), "moe_ffn: reset control words");
+    return step_launch(a, stream);
 }

@@ -1,5 +1,6 @@
-// moe.cuh -- shared definitions of the MoE FFN kernels (moe.cu) and the stack
-// executor (stack.cu).
+// moe.cuh -- shared definitions of the persistent MoE step kernel (moe.cu)
+// and its callers (the MoE block entry points in moe.cu, the stack executor
+// in stack.cu, the no-alloc entry point in noalloc.cu).
 #pragma once
 #include "common.cuh"
 
@@ -12,110 +13,107 @@ constexpr int MOE_HMAX = 4096;   // hidden size
 constexpr int MOE_IMAX = 2048;   // expert intermediate size
 constexpr int MOE_TC = 8;        // (token, expert) pairs per chunk
 constexpr int MOE_ROWTILE = 32;  // gate/up rows per work item (one activation group)
-constexpr int MOE_RT3 = 16;      // down rows (= output rows) per work item
-constexpr int K1_TG = 4;         // tokens per router CTA
+constexpr int MOE_RT3 = 16;      // down rows (= output columns of h) per tile
+constexpr int EP_MAXW = 8;       // expert-parallel ranks
 
-// One chunk of up to MOE_TC pairs of one expert group, with everything the
-// expert kernels need to start their bulk copies: resolved weight pointers,
-// the pairs' first index (pairs of a group are contiguous), their tokens and
-// routing weights.  Written by the router's finalize step; 16-byte aligned so
-// that it can itself be bulk-copied into shared memory.
-struct __align__(16) MoeChunk {
-    const uint8_t *gate, *up, *down;
-    int p0, np, group, pad;
-    uint8_t tok[MOE_TC];
-    float w[MOE_TC];
-    uint8_t pad2[8];
+__host__ __device__ constexpr size_t al16(size_t v) { return (v + 15) / 16 * 16; }
+
+// Lane geometry of the quantised lane dots (qdot.cuh): 4 lanes per
+// super-block, so one row of NB blocks takes 4*NB lanes; wider rows take
+// several column passes (CP), narrower ones share a warp (RPW rows per step).
+template <int QT, int NB>
+struct MGeo {
+    static constexpr int BB = QT == BREAD_QTYPE_Q4_K ? Q4K_BYTES : Q6K_BYTES;
+    static constexpr int LANES_ALL = 4 * NB;
+    static constexpr int CP = LANES_ALL > 32 ? LANES_ALL / 32 : 1;
+    static constexpr int LPR = LANES_ALL > 32 ? 32 : LANES_ALL;
+    static constexpr int RPW = 32 / LPR;
+    static constexpr int ROWB = BB * NB;
+    static constexpr int STEPB = ROWB * RPW;
 };
-static_assert(sizeof(MoeChunk) == 96, "MoeChunk layout");
 
-// Byte offsets of the pieces of a MoE workspace (all 256-byte aligned).
-struct MoeWs {
-    size_t hdr, logits, ssq, score, ridx, rw, sgw, xq, xs, p_token, p_w, chunks, aq, as, total;
-    int GM, PM, CM;
-    static MoeWs make(int T, int H, int I, int E, int k)
+// Weights of one MoE layer as the step kernel reads them.  Routed experts
+// come either from per-expert pointer tables (the reference's
+// weight_cache_t gate_ptrs[e] etc., loader.h:79-84) or, when *_base is set,
+// from contiguous arrays holding experts [lo, hi) at a fixed stride (no
+// pointer loads on the critical path).
+struct StepLayer {
+    const uint8_t *const *gate;  // device tables [E] of per-expert matrices;
+    const uint8_t *const *up;    // NULL entries: expert not held here
+    const uint8_t *const *down;
+    const uint8_t *gate_base, *up_base, *down_base;  // or contiguous experts [lo, hi)
+    size_t gu_stride, d_stride;                      // bytes between consecutive experts
+    const uint8_t *sh_gate, *sh_up, *sh_down;        // shared expert, or NULL
+    const float *W_r;                                // [E x H] fp32 router
+    const __half *w_sg;                              // [H] fp16 shared-gate vector, or NULL
+};
+
+// Control words at the head of the workspace (u64 each): the grid-barrier
+// counter, the exit ticket and the launch epoch.  Zero before the first
+// launch; the last CTA of every launch resets the first two and advances the
+// epoch.
+enum { CTRL_GRID = 0, CTRL_EXIT = 1, CTRL_EPOCH = 2 };
+
+// Phase points recorded per layer and CTA by a profiled launch
+// (StepArgs::stamps, %globaltimer ns).  Consumer thread 0: 0 layer start,
+// 1 logits written, 2 after the router barrier, 3 routing tables built, 4 first
+// activation slot landed, 5 gate/up done, 6 after the gate/up barrier, 7 first
+// down stage landed, 8 down done, 9 layer end.  Producer: 10 routing tables
+// seen, 11 gate/up copies issued, 12 down weight copies issued, 13 next
+// layer's router rows issued, 14 gate/up barrier seen, 15 all down copies
+// issued.
+constexpr int STAMPS = 16;
+constexpr size_t CTRL_BYTES = 256;
+
+// Global scratch of one step launch (byte offsets, each 256-byte aligned).
+struct StepWs {
+    size_t ctrl, logits, score, ssq, xq, xs, aq, as, buf0, buf1, total;
+    int PM;
+    __host__ static StepWs make(int T, int H, int I, int E, int K, bool inter_layer_buffers)
     {
-        MoeWs w;
+        StepWs w;
         size_t o = 0;
         auto take = [&](size_t bytes) {
             const size_t at = o;
             o += (bytes + 255) / 256 * 256;
             return at;
         };
-        w.GM = (E < T * k ? E : T * k) + 1;
-        w.PM = T * (k + 1);
-        w.CM = w.GM + (w.PM + MOE_TC - 1) / MOE_TC;
-        w.hdr = take(64);
+        w.PM = T * (K + 1);
+        w.ctrl = take(CTRL_BYTES);
         w.logits = take((size_t)T * E * 4);
-        w.ssq = take((size_t)T * (H / 32) * 4);
         w.score = take((size_t)T * 4);
-        w.ridx = take((size_t)T * k * 4);
-        w.rw = take((size_t)T * k * 4);
-        w.sgw = take((size_t)T * 4);
+        w.ssq = take((size_t)T * (H / 32) * 4);
         w.xq = take((size_t)T * H * 2);
         w.xs = take((size_t)T * (H / 32) * 4);
-        w.p_token = take((size_t)w.PM * 4);
-        w.p_w = take((size_t)w.PM * 4);
-        w.chunks = take((size_t)w.CM * sizeof(MoeChunk));
-        w.aq = take((size_t)w.PM * (I > 0 ? I : 1) * 2);
+        w.aq = take((size_t)w.PM * (I > 0 ? I : 32) * 2);
         w.as = take((size_t)w.PM * (I > 0 ? I / 32 : 1) * 4);
+        w.buf0 = inter_layer_buffers ? take((size_t)T * H * 4) : 0;
+        w.buf1 = inter_layer_buffers ? take((size_t)T * H * 4) : 0;
         w.total = o;
         return w;
     }
 };
 
-// Header words at MoeWs::hdr.
-enum { HDR_TICKET = 0, HDR_NGROUPS = 1, HDR_NCHUNKS = 2, HDR_NPAIRS = 3 };
-
-// Everything the MoE kernels read or write (passed by value).
-struct MoeArgs {
-    const uint8_t *const *gate;  // device tables [E] (routed experts)
-    const uint8_t *const *up;
-    const uint8_t *const *down;
-    const float *W_r;            // [E x H] fp32
-    const __half *w_sg;          // [H] fp16 or NULL
-    const uint8_t *sh_gate, *sh_up, *sh_down;  // shared expert or NULL
-    int T, H, I, E, top_k;
-    int lo, hi;                  // experts computed here: [lo, hi)
-    int shared_here;             // 1: the shared expert is computed here
-    float norm_eps;              // >= 0: inputs are RMS-normalised first
-    const float *x;              // router / expert input [T x H]
-    float *out;                  // [T x H] accumulated into
-    // workspace
-    int *hdr;
-    float *logits, *ssq, *score;
-    int *ridx;
-    float *rw, *sgw;
-    int16_t *xq;
-    float *xs;
-    int *p_token;
-    float *p_w;
-    MoeChunk *chunks;
-    int16_t *aq;
-    float *as;
-    // optional routing copies
-    int *idx_out;
-    float *w_out, *sg_out;
-    int *stats;  // optional: [groups, pairs] computed here (written by the router)
-    // expert parallel (ep_world > 1): the down kernel stores its partial rows
-    // into every rank's mailbox instead of accumulating into `out`, then
-    // counts one arrival per CTA at every rank (MoeMailbox layout)
-    float *ep_mb[8];
-    int ep_world, ep_rank, ep_slot, ep_tmax;
+// Shared-memory layout of one launch (byte offsets), computed on the host.
+struct StepSmem {
+    uint32_t rbuf, part, xsl, gring, abuf, dring, acc, bars, total;
+    uint32_t r_idx, r_w, r_rinv, r_sgw, r_cnt, r_run, r_off, r_gexp, r_goff, r_gcnt, r_gcpre, r_ptok, r_pw, r_scal, r_ptr, r_chunk;
+    uint32_t xslot, dslot;
+    int NS_G, NS_D, RR, WPR;
 };
 
-// Mailbox of one rank (expert parallel): [MB_SLOTS][world][Tmax x H] fp32
-// partials, arrival counters [MB_SLOTS][8], combine tickets [MB_SLOTS].
+// Expert-parallel mailbox of one rank: [3 slots][world][Tmax x H] fp32
+// partials written by every rank over NVLink, then one u64 arrival counter
+// per slot (monotonic; targets derive from the launch epoch).
 constexpr int MB_SLOTS = 3;
-struct MoeMailbox {
-    size_t flag_off, ticket_off, total;
-    __host__ __device__ static MoeMailbox make(int world, int Tmax, int H)
+struct StepMailbox {
+    size_t ctr_off, total;
+    __host__ __device__ static StepMailbox make(int world, int Tmax, int H)
     {
-        MoeMailbox m;
+        StepMailbox m;
         const size_t data = (size_t)MB_SLOTS * world * Tmax * H * 4;
-        m.flag_off = (data + 255) / 256 * 256;
-        m.ticket_off = m.flag_off + 256;
-        m.total = m.ticket_off + 256;
+        m.ctr_off = (data + 255) / 256 * 256;
+        m.total = m.ctr_off + 256;
         return m;
     }
     __host__ __device__ static size_t data_off(int slot, int src, int world, int Tmax, int H)
@@ -124,15 +122,43 @@ struct MoeMailbox {
     }
 };
 
-void moe_bind_workspace(MoeArgs &a, void *ws, const MoeWs &L);
+// Everything the step kernel reads (passed by value).
+struct StepArgs {
+    StepLayer l0;               // layer 0 when `layers` is NULL
+    const StepLayer *layers;    // device array [L], or NULL (L == 1)
+    int L, T, H, I, E, top_k;
+    int lo, hi;                 // routed experts computed here: [lo, hi)
+    float norm_eps;             // >= 0: each layer's input is RMS-normalised first
+    int route_only;             // 1: routing outputs only (no expert work)
+    int res_is_out;             // 1: y += moe(x) (one block);  0: h <- h + moe(norm(h)) per layer
+    const float *x;             // input of layer 0 [T x H]
+    float *y;                   // output of the last layer [T x H]
+    float *buf[2];              // inter-layer buffers [T x H] (L > 1)
+    // workspace
+    unsigned long long *ctrl;
+    float *logits, *score, *ssq;
+    int16_t *xq;
+    float *xs;
+    int16_t *aq;
+    float *as;
+    // optional outputs (written by CTA 0)
+    int *idx_out;
+    float *w_out, *sg_out;
+    int *stats;                 // [L][2]: expert groups, pairs computed here
+    unsigned long long *stamps; // [L][grid][STAMPS] %globaltimer at phase points of every CTA, or NULL
+    // expert parallel
+    float *ep_mb[EP_MAXW];
+    int ep_world, ep_rank, ep_tmax;
+    StepSmem sm;
+};
+
 int moe_check_shapes(int T, int H, int I, int E, int top_k, bool need_experts);
-// Router + finalize, gate/up + SiLU*mul, down + combine, expert-parallel
-// combine.  All are launched with programmatic dependent launch allowed.
-int moe_launch_route(const MoeArgs &a, cudaStream_t s);
-int moe_launch_gateup(const MoeArgs &a, cudaStream_t s);
-int moe_launch_down(const MoeArgs &a, cudaStream_t s);
-int moe_down_grid(const MoeArgs &a);
-int moe_launch_combine(const MoeArgs &a, float *h, cudaStream_t s);
-int moe_setup_kernels(int H, int I);
+// Binds the workspace pieces of StepWs::make(...) at `ws` into `a`.
+void step_bind_workspace(StepArgs &a, void *ws, const StepWs &L);
+// Computes the shared-memory layout for the current device, sets the kernel
+// attributes once per device and launches the cooperative step kernel.
+int step_launch(StepArgs &a, cudaStream_t s);
+// One-time per-device kernel set-up (call before any stream capture).
+int step_setup(int H, int I);
 
 }  // namespace bread

@@ -68,7 +68,7 @@ extern "C" int bread_moe_ffn_noalloc(const void *const *gate_ptrs, const void *c
                                      float *sg_out, cudaStream_t stream)
 {
     BREAD_TRY(moe_check_shapes(T, H, I, E, top_k, true));
-    const size_t need = MoeWs::make(T, H, I, E, top_k).total;
+    const size_t need = StepWs::make(T, H, I, E, top_k, false).total;
     if (need > NOALLOC_SCRATCH_BYTES)
         return set_error(BREAD_ERR_WORKSPACE,
                          "moe_ffn_noalloc: T=%d H=%d I=%d E=%d top_k=%d need %zu bytes of scratch, the fixed array "

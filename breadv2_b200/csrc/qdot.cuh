@@ -111,7 +111,9 @@ struct XSlice {
 // Q4_K lane (block b, pair g): block elements 64g..64g+63, i.e. sub-blocks 2g
 // (low nibbles of qs[32g..32g+31]) and 2g+1 (high nibbles).
 // xq/xs: the token's int16 values and per-32 scales; e0 = 256*b + 64*g.
-__device__ __forceinline__ void load_slice_q4k(XSlice &X, const int16_t *xq, const float *xs, int e0)
+// rs multiplies the group scales (the RMS-normalisation factor of the token).
+__device__ __forceinline__ void load_slice_q4k(XSlice &X, const int16_t *xq, const float *xs, int e0,
+                                               float rs = 1.0f)
 {
     const int4 *p = reinterpret_cast<const int4 *>(xq + e0);
 #pragma unroll
@@ -128,7 +130,7 @@ __device__ __forceinline__ void load_slice_q4k(XSlice &X, const int16_t *xq, con
         s0 = sum_i16x2(X.v[i], s0);
         s1 = sum_i16x2(X.v[16 + i], s1);
     }
-    const float f0 = xs[e0 >> 5], f1 = xs[(e0 >> 5) + 1];
+    const float f0 = xs[e0 >> 5] * rs, f1 = xs[(e0 >> 5) + 1] * rs;
     X.s[0] = f0;
     X.s[1] = f1 * 0.0625f;  // the high nibbles enter the dot product as 16*q
     X.s[2] = f0 * (float)s0;

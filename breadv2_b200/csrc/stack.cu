@@ -3,13 +3,13 @@
 // for n_layers layers with every expert resident in HBM (no loader.c LRU, no
 // host->device expert streaming).
 //
-// One decode step for T tokens, per layer l:
-//   K1 route (RMS-normalises h on the fly) -> K2 gate/up -> K3 down + combine
-//   and, with world > 1 (expert parallel), K3 stores its partial rows into
-//   every rank's mailbox over NVLink and signals with system-scope atomics;
-//   a combine kernel on each rank then waits (bounded) for all ranks and adds
-//   the partials in rank order, so every rank holds the same bits.
-// The whole step is captured once per (T, h) into a CUDA graph and replayed.
+// One decode step for T tokens is ONE launch of the persistent step kernel
+// (moe.cu): per layer l, h <- h + moe_l(rmsnorm(h)) with grid-wide barriers
+// between the router, gate/up and down phases.  With world > 1 (expert
+// parallel) the down phase stores the rank's partial columns into every
+// rank's mailbox over NVLink and counts arrivals there; the next layer's
+// first phase waits (bounded) for all ranks and adds the partials in rank
+// order, so every rank holds the same bits.
 //
 // Expert parallelism: rank r holds routed experts [r*E/world, (r+1)*E/world)
 // of every layer plus the shared expert of layers l with l % world == r; the
@@ -17,8 +17,6 @@
 // dispatch exchange is needed.
 #include <string.h>
 
-#include <map>
-#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -30,8 +28,6 @@ namespace bread {
 // stream ids of the synthetic tensors: (layer, kind, expert)
 static uint64_t sid(int layer, int kind, int e) { return ((uint64_t)layer << 32) | ((uint64_t)kind << 24) | (uint64_t)e; }
 enum { K_GATE = 0, K_UP = 1, K_DOWN = 2, K_SH_GATE = 3, K_SH_UP = 4, K_SH_DOWN = 5, K_ROUTER = 6, K_SGVEC = 7 };
-
-constexpr int EP_MAXW = 8;
 
 struct LayerW {
     uint8_t *gate, *up, *down;           // local experts, contiguous [n_local x ...]
@@ -50,20 +46,18 @@ struct bread_stack {
     size_t bytes = 0;
     std::vector<void *> allocs;
     std::vector<bread::LayerW> layers;
+    bread::StepLayer *layer_desc = nullptr;  // device array [n_layers] the step kernel reads
     void *ws = nullptr;
-    bread::MoeWs wsl;
+    bread::StepWs wsl;
     float *h_dev = nullptr;  // staging buffer of bread_stack_step_host
     // expert parallel
     uint8_t *mailbox = nullptr;
-    bread::MoeMailbox mbl;
+    bread::StepMailbox mbl;
     bool peers_set = false;
-    cudaStream_t cap = nullptr;  // private stream graphs are captured on
     float *peer_mb[bread::EP_MAXW] = {};
-    std::map<std::pair<int, float *>, cudaGraphExec_t> graphs;
-    int *stats_dev = nullptr;  // [n_layers][2]: groups, pairs of the last step
-    // instrumented replay: events around every kernel of every layer
-    std::vector<cudaEvent_t> ev;
-    std::map<std::pair<int, float *>, cudaGraphExec_t> prof_graphs;
+    int *stats_dev = nullptr;                   // [n_layers][2]: groups, pairs of the last step
+    unsigned long long *stamps_dev = nullptr;   // [n_layers][ctas][STAMPS]: phase points of the last profiled step
+    int ctas = 0;                               // grid of the step kernel (one CTA per SM)
 };
 
 using namespace bread;
@@ -80,10 +74,6 @@ static int stack_alloc(bread_stack *st, void **p, size_t bytes, const char *what
 extern "C" int bread_stack_destroy(bread_stack_t *st)
 {
     if (!st) return BREAD_OK;
-    for (auto &kv : st->graphs) cudaGraphExecDestroy(kv.second);
-    for (auto &kv : st->prof_graphs) cudaGraphExecDestroy(kv.second);
-    for (cudaEvent_t e : st->ev) cudaEventDestroy(e);
-    if (st->cap) cudaStreamDestroy(st->cap);
     for (void *p : st->allocs) cudaFree(p);
     delete st;
     return BREAD_OK;
@@ -163,7 +153,7 @@ extern "C" int bread_stack_create(bread_stack_t **out, const bread_stack_config_
             rc = set_error(BREAD_ERR_CUDA, "stack: upload tables");
     }
     if (!rc) {
-        st->wsl = MoeWs::make(c.max_tokens, H, I, E, c.top_k);
+        st->wsl = StepWs::make(c.max_tokens, H, I, E, c.top_k, true);
         rc = stack_alloc(st, &st->ws, st->wsl.total, "stack: workspace");
         if (!rc && cudaMemsetAsync(st->ws, 0, st->wsl.total, s) != cudaSuccess) rc = set_error(BREAD_ERR_CUDA, "stack: clear workspace");
         void *p = nullptr;
@@ -171,12 +161,39 @@ extern "C" int bread_stack_create(bread_stack_t **out, const bread_stack_config_
         st->h_dev = (float *)p;
         if (!rc) rc = stack_alloc(st, &p, (size_t)c.n_layers * 2 * sizeof(int), "stack: stats");
         st->stats_dev = (int *)p;
+        st->ctas = sm_count();
+        if (!rc) rc = stack_alloc(st, &p, (size_t)c.n_layers * st->ctas * STAMPS * sizeof(unsigned long long), "stack: stamps");
+        st->stamps_dev = (unsigned long long *)p;
     }
-    if (!rc && cudaStreamCreateWithFlags(&st->cap, cudaStreamNonBlocking) != cudaSuccess)
-        rc = set_error(BREAD_ERR_CUDA, "stack: capture stream");
-    if (!rc) rc = moe_setup_kernels(H, I);
+    if (!rc) {
+        // per-layer descriptors the step kernel reads
+        std::vector<StepLayer> d((size_t)c.n_layers);
+        for (int l = 0; l < c.n_layers; ++l) {
+            const LayerW &L = st->layers[l];
+            d[l].gate = L.tab;
+            d[l].up = L.tab + E;
+            d[l].down = L.tab + 2 * E;
+            d[l].gate_base = L.gate;  // local experts are contiguous: no pointer loads
+            d[l].up_base = L.up;
+            d[l].down_base = L.down;
+            d[l].gu_stride = gate_b;
+            d[l].d_stride = down_b;
+            d[l].sh_gate = L.sh_gate;
+            d[l].sh_up = L.sh_up;
+            d[l].sh_down = L.sh_down;
+            d[l].W_r = L.W_r;
+            d[l].w_sg = L.w_sg;
+        }
+        void *p = nullptr;
+        rc = stack_alloc(st, &p, d.size() * sizeof(StepLayer), "stack: layer descriptors");
+        st->layer_desc = (StepLayer *)p;
+        if (!rc && (cudaMemcpyAsync(p, d.data(), d.size() * sizeof(StepLayer), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+                    cudaStreamSynchronize(s) != cudaSuccess))
+            rc = set_error(BREAD_ERR_CUDA, "stack: upload layer descriptors");
+    }
+    if (!rc) rc = step_setup(H, I);
     if (!rc && c.world > 1) {
-        st->mbl = MoeMailbox::make(c.world, c.max_tokens, H);
+        st->mbl = StepMailbox::make(c.world, c.max_tokens, H);
         void *p = nullptr;
         rc = stack_alloc(st, &p, st->mbl.total, "stack: mailbox");
         st->mailbox = (uint8_t *)p;
@@ -230,10 +247,6 @@ extern "C" int bread_stack_set_peers(bread_stack_t *st, void *const *peer_mailbo
         st->peer_mb[r] = static_cast<float *>(peer_mailboxes[r]);
     }
     st->peers_set = true;
-    for (auto &kv : st->graphs) cudaGraphExecDestroy(kv.second);
-    st->graphs.clear();
-    for (auto &kv : st->prof_graphs) cudaGraphExecDestroy(kv.second);
-    st->prof_graphs.clear();
     return BREAD_OK;
 }
 
@@ -265,81 +278,7 @@ extern "C" int bread_ipc_close_handle(void *dev_ptr)
 extern "C" int bread_stack_launches_per_step(const bread_stack_t *st, int T)
 {
     (void)T;
-    if (!st) return 0;
-    return st->cfg.n_layers * (st->cfg.world > 1 ? 4 : 3);
-}
-
-// Mailbox slot of layer l: consecutive layers (also the last and the first
-// of the next step) always use different slots, which is what makes a slot
-// safe to overwrite (see ep_combine_kernel).
-static int mailbox_slot(int l, int L) { return (L & 1) && l == L - 1 ? 2 : (l & 1); }
-
-// ev: NULL, or 5 events per layer recorded before K1, K2, K3, the combine,
-// and at the end of the layer.
-static int stack_enqueue(bread_stack_t *st, float *h, int T, cudaStream_t s, const cudaEvent_t *ev = nullptr)
-{
-    const bread_stack_config_t &c = st->cfg;
-    for (int l = 0; l < c.n_layers; ++l) {
-        const LayerW &L = st->layers[l];
-        MoeArgs a{};
-        a.gate = L.tab;
-        a.up = L.tab + c.n_experts;
-        a.down = L.tab + 2 * c.n_experts;
-        a.W_r = L.W_r;
-        a.w_sg = L.w_sg;
-        a.sh_gate = L.sh_gate;
-        a.sh_up = L.sh_up;
-        a.sh_down = L.sh_down;
-        a.T = T;
-        a.H = c.hidden;
-        a.I = c.inter;
-        a.E = c.n_experts;
-        a.top_k = c.top_k;
-        a.lo = st->lo;
-        a.hi = st->hi;
-        a.shared_here = L.sh_gate != nullptr;
-        a.norm_eps = c.norm_eps;
-        a.x = h;
-        a.out = h;
-        a.stats = st->stats_dev + 2 * l;
-        if (c.world > 1) {
-            a.ep_world = c.world;
-            a.ep_rank = c.rank;
-            a.ep_slot = mailbox_slot(l, c.n_layers);
-            a.ep_tmax = c.max_tokens;
-            for (int r = 0; r < c.world; ++r) a.ep_mb[r] = st->peer_mb[r];
-        }
-        moe_bind_workspace(a, st->ws, st->wsl);
-        if (ev) BREAD_CUDA(cudaEventRecordWithFlags(ev[5 * l + 0], s, cudaEventRecordExternal), "stack: event");
-        BREAD_TRY(moe_launch_route(a, s));
-        if (ev) BREAD_CUDA(cudaEventRecordWithFlags(ev[5 * l + 1], s, cudaEventRecordExternal), "stack: event");
-        BREAD_TRY(moe_launch_gateup(a, s));
-        if (ev) BREAD_CUDA(cudaEventRecordWithFlags(ev[5 * l + 2], s, cudaEventRecordExternal), "stack: event");
-        BREAD_TRY(moe_launch_down(a, s));
-        if (ev) BREAD_CUDA(cudaEventRecordWithFlags(ev[5 * l + 3], s, cudaEventRecordExternal), "stack: event");
-        if (c.world > 1) BREAD_TRY(moe_launch_combine(a, h, s));
-        if (ev) BREAD_CUDA(cudaEventRecordWithFlags(ev[5 * l + 4], s, cudaEventRecordExternal), "stack: event");
-    }
-    return BREAD_OK;
-}
-
-// Captures one step into a graph on the stack's private stream (capture is
-// not allowed on the legacy default stream a caller may use).
-static int capture(bread_stack_t *st, float *h, int T, const cudaEvent_t *ev, cudaGraphExec_t *out)
-{
-    cudaGraph_t g = nullptr;
-    BREAD_CUDA(cudaStreamBeginCapture(st->cap, cudaStreamCaptureModeThreadLocal), "stack: begin capture");
-    const int rc = stack_enqueue(st, h, T, st->cap, ev);
-    const cudaError_t ce = cudaStreamEndCapture(st->cap, &g);
-    if (rc != BREAD_OK) {
-        if (g) cudaGraphDestroy(g);
-        return rc;
-    }
-    if (ce != cudaSuccess) return cuda_status(ce, "stack: end capture");
-    const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
-    cudaGraphDestroy(g);
-    if (ie != cudaSuccess) return cuda_status(ie, "stack: instantiate graph");
-    return BREAD_OK;
+    return st ? 1 : 0;  // one cooperative launch of the step kernel per decode step
 }
 
 static int ready(const bread_stack_t *st, const float *h, int T)
@@ -348,21 +287,43 @@ static int ready(const bread_stack_t *st, const float *h, int T)
     if (T < 1 || T > st->cfg.max_tokens) return set_error(BREAD_ERR_ARG, "stack: T=%d outside 1..%d", T, st->cfg.max_tokens);
     if (st->cfg.world > 1 && !st->peers_set)
         return set_error(BREAD_ERR_STATE, "stack: expert-parallel stack needs bread_stack_set_peers first");
+    if (reinterpret_cast<uintptr_t>(h) & 15) return set_error(BREAD_ERR_ALIGN, "stack: h must be 16-byte aligned");
     return BREAD_OK;
+}
+
+// One decode step: all layers in one launch of the step kernel.
+static int stack_launch(bread_stack_t *st, float *h, int T, cudaStream_t s, unsigned long long *stamps)
+{
+    const bread_stack_config_t &c = st->cfg;
+    StepArgs a{};
+    a.layers = st->layer_desc;
+    a.L = c.n_layers;
+    a.T = T;
+    a.H = c.hidden;
+    a.I = c.inter;
+    a.E = c.n_experts;
+    a.top_k = c.top_k;
+    a.lo = st->lo;
+    a.hi = st->hi;
+    a.norm_eps = c.norm_eps;
+    a.res_is_out = 0;
+    a.x = h;
+    a.y = h;
+    a.stats = st->stats_dev;
+    a.stamps = stamps;
+    a.ep_world = c.world;
+    a.ep_rank = c.rank;
+    a.ep_tmax = c.max_tokens;
+    if (c.world > 1)
+        for (int r = 0; r < c.world; ++r) a.ep_mb[r] = st->peer_mb[r];
+    step_bind_workspace(a, st->ws, st->wsl);
+    return step_launch(a, s);
 }
 
 extern "C" int bread_stack_step(bread_stack_t *st, float *h, int T, cudaStream_t stream)
 {
     BREAD_TRY(ready(st, h, T));
-    const auto key = std::make_pair(T, h);
-    auto it = st->graphs.find(key);
-    if (it == st->graphs.end()) {
-        cudaGraphExec_t ge = nullptr;
-        BREAD_TRY(capture(st, h, T, nullptr, &ge));
-        it = st->graphs.emplace(key, ge).first;
-    }
-    BREAD_CUDA(cudaGraphLaunch(it->second, stream), "stack: graph launch");
-    return BREAD_OK;
+    return stack_launch(st, h, T, stream, nullptr);
 }
 
 extern "C" int bread_stack_profile_step(bread_stack_t *st, float *h, int T, cudaStream_t stream, float *kernel_ms)
@@ -370,23 +331,35 @@ extern "C" int bread_stack_profile_step(bread_stack_t *st, float *h, int T, cuda
     BREAD_TRY(ready(st, h, T));
     if (!kernel_ms) return set_error(BREAD_ERR_ARG, "stack_profile_step: NULL kernel_ms");
     const int L = st->cfg.n_layers;
-    if (st->ev.empty()) {
-        st->ev.resize((size_t)5 * L);
-        for (auto &e : st->ev) BREAD_CUDA(cudaEventCreate(&e), "stack: create event");
-    }
-    const auto key = std::make_pair(T, h);
-    auto it = st->prof_graphs.find(key);
-    if (it == st->prof_graphs.end()) {
-        cudaGraphExec_t ge = nullptr;
-        BREAD_TRY(capture(st, h, T, st->ev.data(), &ge));
-        it = st->prof_graphs.emplace(key, ge).first;
-    }
-    BREAD_CUDA(cudaGraphLaunch(it->second, stream), "stack: graph launch");
+    const size_t n = (size_t)L * st->ctas * STAMPS;
+    // points a CTA never reaches (no work of that kind) read 0
+    BREAD_CUDA(cudaMemsetAsync(st->stamps_dev, 0, n * sizeof(unsigned long long), stream), "stack: clear stamps");
+    BREAD_TRY(stack_launch(st, h, T, stream, st->stamps_dev));
+    std::vector<unsigned long long> t(n);
+    BREAD_CUDA(cudaMemcpyAsync(t.data(), st->stamps_dev, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, stream),
+               "stack: read phase stamps");
     BREAD_CUDA(cudaStreamSynchronize(stream), "stack: profile sync");
-    for (int l = 0; l < L; ++l)
-        for (int k = 0; k < 4; ++k)
-            BREAD_CUDA(cudaEventElapsedTime(kernel_ms + 4 * l + k, st->ev[5 * l + k], st->ev[5 * l + k + 1]),
-                       "stack: elapsed time");
+    // CTA 0's view of layer l: router phase [0,2), gate/up [2,6), down [6,9),
+    // then the gap until the next layer starts (the expert-parallel wait)
+    for (int l = 0; l < L; ++l) {
+        const unsigned long long *p = t.data() + (size_t)l * st->ctas * STAMPS;
+        kernel_ms[4 * l + 0] = (float)(p[2] - p[0]) * 1e-6f;
+        kernel_ms[4 * l + 1] = (float)(p[6] - p[2]) * 1e-6f;
+        kernel_ms[4 * l + 2] = (float)(p[9] - p[6]) * 1e-6f;
+        kernel_ms[4 * l + 3] =
+            l + 1 < L ? (float)(p[(size_t)st->ctas * STAMPS] - p[9]) * 1e-6f : 0.0f;
+    }
+    return BREAD_OK;
+}
+
+extern "C" int bread_stack_profile_stamps(const bread_stack_t *st, unsigned long long *out, size_t n_words, int *ctas)
+{
+    if (!st || !out) return set_error(BREAD_ERR_ARG, "stack_profile_stamps: NULL argument");
+    const size_t n = (size_t)st->cfg.n_layers * st->ctas * STAMPS;
+    if (n_words < n) return set_error(BREAD_ERR_ARG, "stack_profile_stamps: need %zu words", n);
+    BREAD_CUDA(cudaMemcpy(out, st->stamps_dev, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost),
+               "stack: read phase stamps");
+    if (ctas) *ctas = st->ctas;
     return BREAD_OK;
 }
 

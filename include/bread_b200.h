@@ -207,13 +207,24 @@ int bread_stack_step(bread_stack_t *st, float *h, int T, cudaStream_t stream);
 /* Same, from and to HOST memory (pinned for best speed): copies h_in to the
  * device, runs the step and copies the result back, all on `stream`. */
 int bread_stack_step_host(bread_stack_t *st, const float *h_in, float *h_out, int T, cudaStream_t stream);
-/* Kernel launches of one step for T tokens (all layers). */
+/* Kernel launches of one step for T tokens (all layers): 1, the whole step
+ * is one cooperative launch of the persistent step kernel. */
 int bread_stack_launches_per_step(const bread_stack_t *st, int T);
-/* One step like bread_stack_step, from a second graph that records CUDA
- * events around every kernel; synchronises `stream` and writes the duration
- * in ms of the router, gate/up, down and expert-parallel combine kernels
- * (0 with world = 1) of every layer to kernel_ms[4*layer + k], k = 0..3. */
+/* One step like bread_stack_step with phase timestamps recorded by every
+ * CTA; synchronises `stream` and writes CTA 0's durations in ms of the router
+ * phase, the gate/up phase, the down phase and the wait for the next layer's
+ * expert-parallel combine (0 with world = 1) of every layer to
+ * kernel_ms[4*layer + k], k = 0..3. */
 int bread_stack_profile_step(bread_stack_t *st, float *h, int T, cudaStream_t stream, float *kernel_ms);
+/* Raw timestamps (ns, %globaltimer) of the last profiled step:
+ * out[(layer * ctas + cta) * 16 + k].  Consumer points k = 0 layer start,
+ * 1 logits written, 2 after the router barrier, 3 routing tables built,
+ * 4 first activation slot landed, 5 gate/up done, 6 after the gate/up
+ * barrier, 7 first down stage landed, 8 down done, 9 layer end; producer
+ * points 10 routing tables seen, 11 gate/up copies issued, 12 down weight
+ * copies issued, 13 next router rows issued, 14 gate/up barrier seen, 15 all
+ * down copies issued.  *ctas receives the grid size.  Synchronous. */
+int bread_stack_profile_stamps(const bread_stack_t *st, unsigned long long *out, size_t n_words, int *ctas);
 /* Per layer of the last step: expert groups computed here (distinct routed
  * experts + the shared expert) and (token, expert) pairs.  Synchronous. */
 int bread_stack_routing_stats(const bread_stack_t *st, int *groups, int *pairs);

@@ -25,4 +25,6 @@ def test_ep_stack_matches_single_gpu(world):
     res = json.loads(line)
     assert res["device_error"] == 0
     assert res["ranks_bitwise_equal"] and res["replays_equal"]
-    assert res["rel_vs_single_gpu"] < 1e-5
+    # same routing as one GPU (a different expert set would differ by O(1));
+    # only the fp32 summation order of the partials differs
+    assert res["rel_vs_single_gpu"] < 1e-4
