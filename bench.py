@@ -58,12 +58,13 @@ def layer_bytes(groups: int, pairs: int, T: int) -> dict:
 
 STAMP_POINTS = ["start", "logits", "router_barrier", "routed", "x_landed", "gateup_done", "gateup_barrier",
                 "down_landed", "down_done", "end", "p_routed", "p_gateup_issued", "p_down_issued", "p_router_issued",
-                "p_gateup_barrier", "p_down_all_issued"]
+                "p_gateup_barrier", "p_down_all_issued", "quantised", "router_rows", "router_dots", "route_inputs",
+                "topk", "tables", "down_stages", "down_stored"]
 
 
 def layer_timeline(stamps) -> dict:
     """Timeline of a layer over all CTAs from the phase stamps [layers, ctas,
-    16] (ns): median and max over CTAs of each phase point, in us from the
+    24] (ns): median and max over CTAs of each phase point, in us from the
     earliest start of the layer, averaged over layers.  A point a CTA never
     reaches (no work of that kind) stays 0 and is left out of the median."""
     import numpy as np

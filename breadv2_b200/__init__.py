@@ -233,17 +233,17 @@ class ExpertStack:
         return out.reshape(L, 4)
 
     def profile_stamps(self):
-        """Timestamps (ns) of the last profile_step: array [layers, ctas, 16] of
+        """Timestamps (ns) of the last profile_step: array [layers, ctas, 24] of
         the phase points listed in bread_stack_profile_stamps."""
         import numpy as np
 
         L = self.cfg.n_layers
-        n = L * 1024 * 16
+        n = L * 1024 * 24
         buf = np.zeros(n, dtype=np.uint64)
         ctas = ctypes.c_int(0)
         check(lib().bread_stack_profile_stamps(self.handle, buf.ctypes.data_as(ctypes.c_void_p), n, ctypes.byref(ctas)),
               "bread_stack_profile_stamps")
-        return buf[: L * ctas.value * 16].reshape(L, ctas.value, 16)
+        return buf[: L * ctas.value * 24].reshape(L, ctas.value, 24)
 
     def routing_stats(self):
         """Per layer of the last step: (expert groups computed here, token-expert pairs)."""

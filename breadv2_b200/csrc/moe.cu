@@ -182,6 +182,18 @@ struct Ring {
             used = 1;
         }
     }
+    // Cursor k positions ahead (0 <= k <= ns): at most one wrap.
+    __device__ __forceinline__ Ring ahead(int k, int ns) const
+    {
+        Ring r = *this;
+        r.slot += k;
+        if (r.slot >= ns) {
+            r.slot -= ns;
+            r.phase ^= 1;
+            r.used = 1;
+        }
+        return r;
+    }
 };
 
 // Matrix k (0 gate, 1 up, 2 down) of expert e (E = the shared expert).
@@ -236,7 +248,8 @@ __device__ __forceinline__ ChunkInfo chunk_search(const RouteTabs &R, int c)
 // expert (all T tokens), then the routed experts held here by ascending id,
 // pairs token-major inside each group.
 template <int PER>
-__device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const RouteTabs &R, int l, bool cta0)
+__device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const RouteTabs &R, int l, bool cta0,
+                             unsigned long long *st)
 {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = a.T, H = a.H, E = a.E, K = a.top_k, HG = H / 32;
@@ -257,53 +270,50 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
         const float score = Ld.w_sg ? __ldcg(a.score + t) : 0.0f;
         ss = warp_sum(ss);
         const float r = a.norm_eps >= 0.0f ? rsqrtf(ss / (float)H + a.norm_eps) : 1.0f;
-        float m = -INFINITY;
+        if (st && tid == 0) st[19] = globaltimer();
+        // top-k by repeated argmax over the RMS-scaled logits.  The softmax is
+        // monotonic, so this selects what cpu_topk selects on the
+        // probabilities (strict >: the lowest index wins ties); and the
+        // renormalised weights p_k / sum(p_top) = exp(l_k - l_max) / sum
+        // exp(l_top - l_max) need no full softmax.  Keys: the float bits made
+        // order-preserving as unsigned (0 = taken or no expert); one warp max
+        // finds the value, one warp min the lowest index holding it.
+        unsigned key[PER];
 #pragma unroll
         for (int j = 0; j < PER; ++j) {
-            p[j] *= r;
-            m = fmaxf(m, p[j]);
+            const unsigned b = __float_as_uint(p[j] * r);
+            key[j] = (lane + 32 * j) < E ? (b & 0x80000000u ? ~b : b | 0x80000000u) : 0u;
         }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float s = 0.0f;
-#pragma unroll
-        for (int j = 0; j < PER; ++j) {
-            p[j] = (lane + 32 * j) < E ? expf(p[j] - m) : 0.0f;
-            s += p[j];
-        }
-        s = warp_sum(s);
-#pragma unroll
-        for (int j = 0; j < PER; ++j) p[j] = (lane + 32 * j) < E ? p[j] / s : -1.0f;
-        unsigned used = 0;
-        float wsum = 0.0f, my_w = 0.0f;
+        float my_l = 0.0f, lmax = 0.0f;
         int my_i = 0;
         for (int k = 0; k < K; ++k) {
-            float bv = -1e30f;
-            int bi = 0x7fffffff;
+            unsigned best = 0;
 #pragma unroll
-            for (int j = 0; j < PER; ++j)
-                if (!((used >> j) & 1u) && p[j] > bv) {
-                    bv = p[j];
-                    bi = lane + 32 * j;
-                }
+            for (int j = 0; j < PER; ++j) best = key[j] > best ? key[j] : best;
+            const unsigned mk = __reduce_max_sync(0xffffffffu, best);
+            unsigned cand = 0xffffffffu;
 #pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
+            for (int j = PER - 1; j >= 0; --j)
+                if (key[j] == mk) cand = (unsigned)(lane + 32 * j);
+            const unsigned bi = __reduce_min_sync(0xffffffffu, cand);
+            if ((int)(bi & 31) == lane) {
+#pragma unroll
+                for (int j = 0; j < PER; ++j)
+                    if (j == (int)(bi >> 5)) key[j] = 0;
             }
-            if ((bi & 31) == lane) used |= 1u << (bi >> 5);
+            const float lv = __uint_as_float(mk & 0x80000000u ? mk & 0x7fffffffu : ~mk);
+            if (k == 0) lmax = lv;
             if (lane == k) {
-                my_w = bv;
-                my_i = bi;
+                my_l = lv;
+                my_i = (int)bi;
             }
-            wsum += bv;
         }
+        const float my_e = lane < K ? expf(my_l - lmax) : 0.0f;
+        const float wsum = warp_sum(my_e);
+        const float my_w = my_e / wsum;
+        if (st && tid == 0) st[20] = globaltimer();
         if (lane < K) {
-            const float w = wsum > 0.0f ? my_w / wsum : my_w;
+            const float w = my_w;
             R.idx[t * K + lane] = my_i;
             R.w[t * K + lane] = w;
             if (cta0 && a.idx_out) a.idx_out[t * K + lane] = my_i;
@@ -321,13 +331,16 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
 
     const int P = T * K;
     if (P <= 32) {
-        // Few pairs (decode): one warp ranks them directly.  Lane q holds pair
-        // q = (token q / K, slot q % K); same tables as the general path below.
+        // Few pairs (decode): one warp builds the tables with a handful of
+        // warp-wide operations.  Lane q holds pair q = (token q / K, slot
+        // q % K).  Groups: the shared expert first, then the routed experts in
+        // order of their first pair (a fixed order, so every CTA and every
+        // rank builds the same tables); pairs token-major inside each group.
         if (warp == 0) {
             const int hs = Ld.sh_gate ? 1 : 0;
             const int hsc = hs ? (T + MOE_TC - 1) / MOE_TC : 0;
             const int pb = hs ? T : 0;
-            int e = 0x7fffffff;
+            int e = -1 - lane;  // distinct dummies for lanes without a local pair
             float w = 0.0f;
             bool loc = false;
             if (lane < P) {
@@ -338,48 +351,47 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
                     loc = true;
                 }
             }
-            int before = 0;  // earlier pairs of the same expert
-            for (int j = 0; j < P; ++j) before += (__shfl_sync(0xffffffffu, e, j) == e && j < lane) ? 1 : 0;
+            const unsigned lt = (1u << lane) - 1u;
+            const unsigned peers = __match_any_sync(0xffffffffu, e);
+            const int before = __popc(peers & lt), same = __popc(peers);
             const bool first = loc && before == 0;
-            int less = 0, dless = 0, same = 0;
-            for (int j = 0; j < P; ++j) {
-                const int ej = __shfl_sync(0xffffffffu, e, j);
-                const int fj = __shfl_sync(0xffffffffu, first ? 1 : 0, j);
-                less += ej < e ? 1 : 0;
-                dless += (ej < e && fj) ? 1 : 0;
-                same += ej == e ? 1 : 0;
-            }
-            const int chn = first ? (same + MOE_TC - 1) / MOE_TC : 0;
-            int cpre = 0;
-            for (int j = 0; j < P; ++j) {
-                const int ej = __shfl_sync(0xffffffffu, e, j);
-                const int cj = __shfl_sync(0xffffffffu, chn, j);
-                cpre += ej < e ? cj : 0;
-            }
-            if (loc) {
-                const int pos = pb + less + before;
-                R.ptok[pos] = lane / K;
-                R.pw[pos] = w;
-                if (first) {
-                    const int g = hs + dless;
-                    R.gexp[g] = e;
-                    R.goff[g] = pb + less;
-                    R.gcnt[g] = same;
-                    R.gcpre[g] = hsc + cpre;
-                    for (int k = 0; k < chn; ++k)
-                        R.chunk[hsc + cpre + k] = make_int4(e, pb + less + MOE_TC * k, min(MOE_TC, same - MOE_TC * k), 0);
-                    if (!Ld.gate_base) {
-                        R.ptr[3 * (e - a.lo) + 0] = expert_ptr(Ld.gate, nullptr, e, E);
-                        R.ptr[3 * (e - a.lo) + 1] = expert_ptr(Ld.up, nullptr, e, E);
-                        R.ptr[3 * (e - a.lo) + 2] = expert_ptr(Ld.down, nullptr, e, E);
-                    }
+            const unsigned firsts = __ballot_sync(0xffffffffu, first);
+            const int g = hs + __popc(firsts & lt);  // group of this lane's expert (valid on first lanes)
+            // exclusive prefix over first lanes of (pairs, chunks) of their group
+            int vp = first ? same : 0, vc = first ? (same + MOE_TC - 1) / MOE_TC : 0;
+            int ip = vp, ic = vc;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int tp = __shfl_up_sync(0xffffffffu, ip, o);
+                const int tc = __shfl_up_sync(0xffffffffu, ic, o);
+                if (lane >= o) {
+                    ip += tp;
+                    ic += tc;
                 }
             }
-            const int ngr = __popc(__ballot_sync(0xffffffffu, first));
-            const int npl = __popc(__ballot_sync(0xffffffffu, loc));
-            int nchr = chn;
-#pragma unroll
-            for (int o = 16; o; o >>= 1) nchr += __shfl_xor_sync(0xffffffffu, nchr, o);
+            const int xp = ip - vp, xc = ic - vc;
+            const int f = __ffs(peers) - 1;  // first lane of this lane's expert
+            const int goff = pb + __shfl_sync(0xffffffffu, xp, f);
+            if (loc) {
+                R.ptok[goff + before] = lane / K;
+                R.pw[goff + before] = w;
+            }
+            if (first) {
+                R.gexp[g] = e;
+                R.goff[g] = goff;
+                R.gcnt[g] = same;
+                R.gcpre[g] = hsc + xc;
+                for (int k = 0; k < vc; ++k)
+                    R.chunk[hsc + xc + k] = make_int4(e, goff + MOE_TC * k, min(MOE_TC, same - MOE_TC * k), 0);
+                if (!Ld.gate_base) {
+                    R.ptr[3 * (e - a.lo) + 0] = expert_ptr(Ld.gate, nullptr, e, E);
+                    R.ptr[3 * (e - a.lo) + 1] = expert_ptr(Ld.up, nullptr, e, E);
+                    R.ptr[3 * (e - a.lo) + 2] = expert_ptr(Ld.down, nullptr, e, E);
+                }
+            }
+            const int ngr = __popc(firsts);
+            const int npl = __shfl_sync(0xffffffffu, ip, 31);
+            const int nchr = __shfl_sync(0xffffffffu, ic, 31);
             if (hs) {
                 for (int t = lane; t < T; t += 32) {
                     R.ptok[t] = t;
@@ -405,6 +417,7 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
                 }
             }
         }
+        if (st && tid == 0) st[21] = globaltimer();
         named_sync(BAR_CONS, ST_CONS);
         return;
     }
@@ -594,10 +607,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
 
     if (warp == 8) {
         // ================================================================ producer
-        const bool P0 = lane == 0;
+        // All 32 lanes run the same control flow; the copies of different
+        // ring slots are issued by different lanes in parallel (a single
+        // thread's dependent address arithmetic costs several hundred ns per
+        // copy).
         Ring gR, dR;   // gate/up and down rings, continued across layers
         int nX = 0;    // activation slots used (2 slots)
-        auto pstamp = [&](int l, int k) { a.stamps[((size_t)l * G + bx) * STAMPS + k] = globaltimer(); };
+        auto pstamp = [&](int l, int k) {
+            if (a.stamps && lane == 0) a.stamps[((size_t)l * G + bx) * STAMPS + k] = globaltimer();
+        };
         // Router rows of layer l (and the shared-gate vector as row E) -> rbuf.
         auto issue_router = [&](int l) {
             const StepLayer Ld = layer_desc(a, l);
@@ -606,22 +624,24 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 const int r = bx * m.RR + rl;
                 bytes += r < E ? H * 4 : (r == E && Ld.w_sg ? H * 2 : 0);
             }
-            if (!bytes) {
-                mbar_arrive(rbar);
-                return;
+            if (lane == 0) {
+                if (bytes)
+                    mbar_arrive_expect_tx(rbar, bytes);
+                else
+                    mbar_arrive(rbar);
             }
-            mbar_arrive_expect_tx(rbar, bytes);
-            for (int rl = 0; rl < m.RR; ++rl) {
-                const int r = bx * m.RR + rl;
+            __syncwarp();
+            const int r = bx * m.RR + lane;
+            if (lane < m.RR) {
                 if (r < E)
-                    bulk_g2s(rbuf + (size_t)rl * H, Ld.W_r + (size_t)r * H, H * 4, rbar);
+                    bulk_g2s(rbuf + (size_t)lane * H, Ld.W_r + (size_t)r * H, H * 4, rbar);
                 else if (r == E && Ld.w_sg)
-                    bulk_g2s(rbuf + (size_t)rl * H, Ld.w_sg, H * 2, rbar);
+                    bulk_g2s(rbuf + (size_t)lane * H, Ld.w_sg, H * 2, rbar);
             }
         };
-        // One gate/up sub-stage (SR gate rows + SR up rows from row r0) at the
-        // ring cursor g.
-        auto issue_gu = [&](Ring &g, const uint8_t *gb, const uint8_t *ub, size_t r0) {
+        // One gate/up sub-stage (SR gate rows + SR up rows from row r0) at ring
+        // cursor g (called by the issuing lane).
+        auto issue_gu = [&](const Ring &g, const uint8_t *gb, const uint8_t *ub, size_t r0) {
             if (g.used) swait(gempty + g.slot, (unsigned)(g.phase ^ 1));
             const unsigned bytes = (unsigned)(C::SR * GH::ROWB);
             uint8_t *dst = gring + (size_t)g.slot * C::STB;
@@ -633,7 +653,6 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 flag_error(DEVERR_ROUTE);
                 mbar_arrive(gfull + g.slot);
             }
-            g.next(NS_G);
         };
         // The shared expert's pairs are the first chunks of every layer, so a
         // CTA whose first item is a shared one knows its rows before routing:
@@ -642,108 +661,106 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             const StepLayer Ld = layer_desc(a, l);
             if (a.route_only || !Ld.sh_gate || bx >= ((T + MOE_TC - 1) / MOE_TC) * R) return 0;
             const int npre = C::SPI < NS_G ? C::SPI : NS_G;
-            Ring g = gR;
-            for (int s = 0; s < npre; ++s)
-                issue_gu(g, Ld.sh_gate, Ld.sh_up, (size_t)(bx % R) * MOE_ROWTILE + (size_t)s * C::SR);
+            if (lane < npre)
+                issue_gu(gR.ahead(lane, NS_G), Ld.sh_gate, Ld.sh_up,
+                         (size_t)(bx % R) * MOE_ROWTILE + (size_t)lane * C::SR);
+            __syncwarp();
             return npre;
         };
-        int npre = 0;
-        if (P0) {
-            issue_router(0);
-            npre = preissue_shared(0);
-        }
+        issue_router(0);
+        int npre = preissue_shared(0);
         for (int l = 0; l < a.L; ++l) {
             named_sync(BAR_ALL, ST_THREADS);  // routing tables of layer l are ready
             if (a.route_only) break;
-            if (P0) {
-                if (a.stamps) pstamp(l, 10);
-                const StepLayer Ld = layer_desc(a, l);
-                fence_proxy_async_global();
-                const int nch = RT.scal[1];
-                // gate/up items (chunk c, row tile rt): activations of the
-                // chunk's tokens + 32 gate and up rows in sub-stages
-                for (int it = bx; it < nch * R; it += G, ++nX) {
-                    const int c = it / R, rt = it % R;  // R: a power of two
-                    const ChunkInfo ci = chunk_info(RT, c);
-                    const int xs_ = nX & 1;
+            pstamp(l, 10);
+            const StepLayer Ld = layer_desc(a, l);
+            fence_proxy_async_global();
+            const int nch = RT.scal[1];
+            // gate/up items (chunk c, row tile rt): activations of the chunk's
+            // tokens + 32 gate and up rows in sub-stages
+            for (int it = bx; it < nch * R; it += G, ++nX) {
+                const int c = it / R, rt = it % R;  // R: a power of two
+                const ChunkInfo ci = chunk_info(RT, c);
+                const int xs_ = nX & 1;
+                if (lane == 0) {
                     if (nX >= 2) swait(xempty + xs_, (unsigned)(((nX >> 1) - 1) & 1));
-                    uint8_t *xb = xsl + (size_t)xs_ * m.xslot;
                     mbar_arrive_expect_tx(xfull + xs_, (unsigned)(ci.np * C::XTOK));
-                    for (int j = 0; j < ci.np; ++j) {
-                        const int t = RT.ptok[ci.p0 + j];
-                        bulk_g2s(xb + (size_t)j * H * 2, a.xq + (size_t)t * H, H * 2, xfull + xs_);
-                        bulk_g2s(xb + (size_t)TC * H * 2 + (size_t)j * (H / 8), a.xs + (size_t)t * (H / 32), H / 8,
-                                 xfull + xs_);
-                    }
-                    const uint8_t *gb = mat_ptr(RT, Ld, a, ci.e, 0);
-                    const uint8_t *ub = mat_ptr(RT, Ld, a, ci.e, 1);
-                    for (int s = 0; s < C::SPI; ++s) {
-                        if (it == bx && s < npre) {  // copied during the previous layer
-                            gR.next(NS_G);
-                            continue;
-                        }
-                        issue_gu(gR, gb, ub, (size_t)rt * MOE_ROWTILE + (size_t)s * C::SR);
-                    }
                 }
-                npre = 0;
-                if (a.stamps) pstamp(l, 11);
-                // down stages (tile it3, chunk c), tile-major: the weights depend
-                // only on the routing, so the first NS_D go out now and are in
-                // flight while the gate/up items compute; the intermediate
-                // follows after the grid barrier
-                auto issue_dw = [&](Ring &d, const ChunkInfo &ci, int it3) {
-                    if (d.used) swait(dempty + d.slot, (unsigned)(d.phase ^ 1));
-                    const uint8_t *db = mat_ptr(RT, Ld, a, ci.e, 2);
-                    if (db && !(reinterpret_cast<uintptr_t>(db) & 15)) {
-                        mbar_arrive_expect_tx(dw + d.slot, (unsigned)C::WB);
-                        bulk_g2s(dring + (size_t)d.slot * m.dslot, db + (size_t)it3 * MOE_RT3 * GI::ROWB,
-                                 (unsigned)C::WB, dw + d.slot);
-                    } else {
-                        flag_error(DEVERR_ROUTE);
-                        mbar_arrive(dw + d.slot);
-                    }
-                };
-                auto issue_da = [&](const Ring &d, const ChunkInfo &ci) {
-                    uint8_t *st = dring + (size_t)d.slot * m.dslot + C::WB;
-                    mbar_arrive_expect_tx(da + d.slot, (unsigned)(ci.np * C::ATOK));
-                    bulk_g2s(st, a.aq + (size_t)ci.p0 * I, (unsigned)(ci.np * I * 2), da + d.slot);
-                    bulk_g2s(st + (size_t)TC * I * 2, a.as + (size_t)ci.p0 * (I / 32), (unsigned)(ci.np * (I / 8)),
-                             da + d.slot);
-                };
-                const Ring d0 = dR;
-                int dpre = 0;
-                {
-                    Ring d = d0;
-                    for (int it3 = bx; it3 < NT && dpre < NS_D; it3 += G)
-                        for (int c = 0; c < nch && dpre < NS_D; ++c, ++dpre) {
-                            issue_dw(d, chunk_info(RT, c), it3);
-                            d.next(NS_D);
-                        }
+                __syncwarp();
+                if (lane < ci.np) {
+                    uint8_t *xb = xsl + (size_t)xs_ * m.xslot;
+                    const int t = RT.ptok[ci.p0 + lane];
+                    bulk_g2s(xb + (size_t)lane * H * 2, a.xq + (size_t)t * H, H * 2, xfull + xs_);
+                    bulk_g2s(xb + (size_t)TC * H * 2 + (size_t)lane * (H / 8), a.xs + (size_t)t * (H / 32), H / 8,
+                             xfull + xs_);
                 }
-                if (a.stamps) pstamp(l, 12);
-                if (l + 1 < a.L) issue_router(l + 1);  // consumers are past phase A
-                if (a.stamps) pstamp(l, 13);
-                // the intermediate of every CTA is complete after grid barrier (phase B)
+                const uint8_t *gb = mat_ptr(RT, Ld, a, ci.e, 0);
+                const uint8_t *ub = mat_ptr(RT, Ld, a, ci.e, 1);
+                for (int s0 = 0; s0 < C::SPI; s0 += NS_G) {  // batches of distinct slots
+                    const int nb = C::SPI - s0 < NS_G ? C::SPI - s0 : NS_G;
+                    const int s = s0 + lane;
+                    if (lane < nb && !(it == bx && s < npre))  // (else copied during the previous layer)
+                        issue_gu(gR.ahead(lane, NS_G), gb, ub, (size_t)rt * MOE_ROWTILE + (size_t)s * C::SR);
+                    gR = gR.ahead(nb, NS_G);
+                    __syncwarp();
+                }
+            }
+            npre = 0;
+            pstamp(l, 11);
+            // down stages n = (tile, chunk), tile-major: the weights depend only
+            // on the routing, so the first NS_D go out now and are in flight
+            // while the gate/up items compute; the intermediate follows after
+            // the grid barrier
+            const int my_tiles = bx < NT ? (NT - 1 - bx) / G + 1 : 0;
+            const int nds = my_tiles * nch;
+            const int dpre = nds < NS_D ? nds : NS_D;
+            auto issue_dw = [&](const Ring &d, int n) {
+                if (d.used) swait(dempty + d.slot, (unsigned)(d.phase ^ 1));
+                const ChunkInfo ci = chunk_info(RT, n % nch);
+                const int it3 = bx + (n / nch) * G;
+                const uint8_t *db = mat_ptr(RT, Ld, a, ci.e, 2);
+                if (db && !(reinterpret_cast<uintptr_t>(db) & 15)) {
+                    mbar_arrive_expect_tx(dw + d.slot, (unsigned)C::WB);
+                    bulk_g2s(dring + (size_t)d.slot * m.dslot, db + (size_t)it3 * MOE_RT3 * GI::ROWB, (unsigned)C::WB,
+                             dw + d.slot);
+                } else {
+                    flag_error(DEVERR_ROUTE);
+                    mbar_arrive(dw + d.slot);
+                }
+            };
+            auto issue_da = [&](const Ring &d, int n) {
+                const ChunkInfo ci = chunk_info(RT, n % nch);
+                uint8_t *st = dring + (size_t)d.slot * m.dslot + C::WB;
+                mbar_arrive_expect_tx(da + d.slot, (unsigned)(ci.np * C::ATOK));
+                bulk_g2s(st, a.aq + (size_t)ci.p0 * I, (unsigned)(ci.np * I * 2), da + d.slot);
+                bulk_g2s(st + (size_t)TC * I * 2, a.as + (size_t)ci.p0 * (I / 32), (unsigned)(ci.np * (I / 8)),
+                         da + d.slot);
+            };
+            if (lane < dpre) issue_dw(dR.ahead(lane, NS_D), lane);
+            __syncwarp();
+            pstamp(l, 12);
+            if (l + 1 < a.L) issue_router(l + 1);  // consumers are past phase A
+            pstamp(l, 13);
+            // the intermediate of every CTA is complete after grid barrier (phase B)
+            if (lane == 0) {
                 const int bidx = ep ? 2 * l + 1 : 3 * l + 1;
                 wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(bidx + 1) * G, false, GRID_WAIT_NS);
-                fence_proxy_async_global();
-                if (a.stamps) pstamp(l, 14);
-                {
-                    Ring d = d0;
-                    int n = 0;
-                    for (int it3 = bx; it3 < NT; it3 += G)
-                        for (int c = 0; c < nch; ++c, ++n) {
-                            const ChunkInfo ci = chunk_info(RT, c);
-                            if (n >= dpre) issue_dw(d, ci, it3);
-                            issue_da(d, ci);
-                            d.next(NS_D);
-                        }
-                    dR = d;
-                }
-                if (a.stamps) pstamp(l, 15);
-                if (l + 1 < a.L) npre = preissue_shared(l + 1);
             }
             __syncwarp();
+            fence_proxy_async_global();
+            pstamp(l, 14);
+            for (int n0 = 0; n0 < nds; n0 += NS_D) {  // batches of distinct slots
+                const int nb = nds - n0 < NS_D ? nds - n0 : NS_D;
+                if (lane < nb) {
+                    const Ring d = dR.ahead(lane, NS_D);
+                    if (n0 + lane >= dpre) issue_dw(d, n0 + lane);
+                    issue_da(d, n0 + lane);
+                }
+                dR = dR.ahead(nb, NS_D);
+                __syncwarp();
+            }
+            pstamp(l, 15);
+            if (l + 1 < a.L) npre = preissue_shared(l + 1);
         }
         return;
     }
@@ -774,10 +791,22 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 for (int r = 0; r < a.ep_world; ++r) v += __ldcv(pmb + (size_t)r * TH + i);
             return v;
         };
+        auto xin4 = [&](size_t i) -> float4 {  // i: a multiple of 4
+            float4 v = __ldcg(reinterpret_cast<const float4 *>(src + i));
+            if (pmb)
+                for (int r = 0; r < a.ep_world; ++r) {
+                    const float4 q = __ldcv(reinterpret_cast<const float4 *>(pmb + (size_t)r * TH + i));
+                    v.x += q.x;
+                    v.y += q.y;
+                    v.z += q.z;
+                    v.w += q.w;
+                }
+            return v;
+        };
         // (1) this CTA's share of the int16 quantisation (+ group sums of squares)
         {
             const int ngr = T * (H / 32);
-            for (int gi = bx * 8 + warp; gi < ngr; gi += G * 8) {
+            for (int gi = (G - 1 - bx) * 8 + warp; gi < ngr; gi += G * 8) {
                 const float v = xin((size_t)gi * 32 + lane);
                 const float ss = warp_sum(v * v);
                 if (lane == 0) a.ssq[gi] = ss;
@@ -785,6 +814,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 a.xq[(size_t)gi * 32 + lane] = (int16_t)q;
             }
         }
+        if (stamp) stamp_at(l, 16);
         // (2) EP: the owner of each column tile materialises this layer's input
         if (pmb) {
             float *dst = const_cast<float *>(in_of(a, l));
@@ -796,6 +826,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         }
         // (3) router rows of this CTA (row E = fp16 shared-gate vector)
         swait(rbar, (unsigned)(l & 1));
+        if (stamp) stamp_at(l, 17);
         {
             const int rl = warp / m.WPR, qt = warp % m.WPR;
             const int row = bx * m.RR + rl;
@@ -804,17 +835,60 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             if (row < nrows) {
                 const float *wr = rbuf + (size_t)rl * H;
                 const __half *wh = reinterpret_cast<const __half *>(wr);
-                for (int t = 0; t < T; ++t) {
-                    float s = 0.0f;
-#pragma unroll 4
-                    for (int c = c0 + lane; c < c0 + seg; c += 32) {
-                        const float w = row < E ? wr[c] : __half2float(wh[c]);
-                        s = fmaf(w, xin((size_t)t * H + c), s);
+                if ((seg & 127) == 0) {
+                    // float4 per lane, 4 per 512 columns: 2 tokens per pass,
+                    // every load in flight before the first use
+                    const float4 *w4 = reinterpret_cast<const float4 *>(wr);
+                    for (int t0 = 0; t0 < T; t0 += 2) {
+                        const bool two = t0 + 1 < T;
+                        float s0 = 0.0f, s1 = 0.0f;
+                        for (int cb = c0; cb < c0 + seg; cb += 512) {
+                            float4 x0[4], x1[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const int c = cb + 4 * lane + 128 * j;
+                                const bool in = c < c0 + seg;
+                                x0[j] = in ? xin4((size_t)t0 * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                                x1[j] = (in && two) ? xin4((size_t)(t0 + 1) * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const int c = cb + 4 * lane + 128 * j;
+                                if (c < c0 + seg) {
+                                    float4 w;
+                                    if (row < E) {
+                                        w = w4[c >> 2];
+                                    } else {
+                                        const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(wh + c));
+                                        const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(wh + c + 2));
+                                        w = make_float4(lo.x, lo.y, hi.x, hi.y);
+                                    }
+                                    s0 = fmaf(w.x, x0[j].x, fmaf(w.y, x0[j].y, fmaf(w.z, x0[j].z, fmaf(w.w, x0[j].w, s0))));
+                                    s1 = fmaf(w.x, x1[j].x, fmaf(w.y, x1[j].y, fmaf(w.z, x1[j].z, fmaf(w.w, x1[j].w, s1))));
+                                }
+                            }
+                        }
+                        s0 = warp_sum(s0);
+                        s1 = warp_sum(s1);
+                        if (lane == 0) {
+                            part[(rl * m.WPR + qt) * T + t0] = s0;
+                            if (two) part[(rl * m.WPR + qt) * T + t0 + 1] = s1;
+                        }
                     }
-                    s = warp_sum(s);
-                    if (lane == 0) part[(rl * m.WPR + qt) * T + t] = s;
+                } else {
+                    // narrow segments (H / warps-per-row < 128): scalar loads
+                    for (int t = 0; t < T; ++t) {
+                        float s0 = 0.0f;
+                        for (int c = c0 + lane; c < c0 + seg; c += 32) {
+                            const float w = row < E ? wr[c] : __half2float(wh[c]);
+                            s0 = fmaf(w, xin((size_t)t * H + c), s0);
+                        }
+                        s0 = warp_sum(s0);
+                        if (lane == 0) part[(rl * m.WPR + qt) * T + t] = s0;
+                    }
                 }
             }
+            if (stamp) stamp_at(l, 18);
             named_sync(BAR_CONS, ST_CONS);
             for (int i = tid; i < m.RR * T; i += ST_CONS) {
                 const int r_l = i / T, t = i % T, rr = bx * m.RR + r_l;
@@ -833,10 +907,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         if (stamp) stamp_at(l, 2);
 
         // ------------------------------------------------------------ phase B
+        unsigned long long *st_l = stamp ? a.stamps + ((size_t)l * G + bx) * STAMPS : nullptr;
         if (E <= 256)
-            route_tables<8>(a, Ld, RT, l, bx == 0);
+            route_tables<8>(a, Ld, RT, l, bx == 0, st_l);
         else
-            route_tables<MOE_EMAX / 32>(a, Ld, RT, l, bx == 0);
+            route_tables<MOE_EMAX / 32>(a, Ld, RT, l, bx == 0, st_l);
         if (stamp) stamp_at(l, 3);
         named_sync(BAR_ALL, ST_THREADS);
         if (a.route_only) break;
@@ -908,6 +983,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             const Q6Lane L6 = q6_lane(((rho * NBI + bb) & 1) ? 2 : 0, sub & 1);
             float *my_acc = acc + (size_t)warp * T * MOE_RT3;
             for (int it3 = bx; it3 < NT; it3 += G) {
+                // residual of this tile's columns, loaded before the stages
+                float rv[MOE_TMAX * MOE_RT3 / ST_CONS];
+#pragma unroll
+                for (int k = 0; k < MOE_TMAX * MOE_RT3 / ST_CONS; ++k) {
+                    const int i = tid + k * ST_CONS;
+                    rv[k] = (!ep && i < T * MOE_RT3)
+                                ? __ldcg(res + (size_t)(i / MOE_RT3) * H + (size_t)it3 * MOE_RT3 + i % MOE_RT3)
+                                : 0.0f;
+                }
                 for (int c = 0; c < nch; ++c, dR.next(NS_D)) {
                     const int slot = dR.slot;
                     const unsigned par = (unsigned)dR.phase;
@@ -945,8 +1029,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                         if (lane == 0) mbar_arrive(dempty + slot);
                     }
                 }
+                if (stamp) stamp_at(l, 22);
                 named_sync(BAR_CONS, ST_CONS);
-                for (int i = tid; i < T * MOE_RT3; i += ST_CONS) {
+#pragma unroll
+                for (int k = 0; k < MOE_TMAX * MOE_RT3 / ST_CONS; ++k) {
+                    const int i = tid + k * ST_CONS;
+                    if (i >= T * MOE_RT3) continue;
                     const int t = i / MOE_RT3, r = i % MOE_RT3;
                     float s = 0.0f;
 #pragma unroll
@@ -960,9 +1048,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                         const size_t off = mb_slot_off(slot_l, a) + (size_t)a.ep_rank * TH + oi;
                         for (int p = 0; p < a.ep_world; ++p) a.ep_mb[p][off] = s;
                     } else {
-                        out[oi] = __ldcg(res + oi) + s;
+                        out[oi] = rv[k] + s;
                     }
                 }
+                if (stamp) stamp_at(l, 23);
                 if (ep) {
                     __threadfence_system();
                     named_sync(BAR_CONS, ST_CONS);

@@ -61,8 +61,11 @@ enum { CTRL_GRID = 0, CTRL_EXIT = 1, CTRL_EPOCH = 2 };
 // down stage landed, 8 down done, 9 layer end.  Producer: 10 routing tables
 // seen, 11 gate/up copies issued, 12 down weight copies issued, 13 next
 // layer's router rows issued, 14 gate/up barrier seen, 15 all down copies
-// issued.
-constexpr int STAMPS = 16;
+// issued.  Consumer thread 0 again: 16 quantisation share done, 17 router rows
+// landed, 18 router dots done, 19 routing inputs read, 20 top-k done, 21
+// tables built (= 3 before the chunk table), 22 down stages done, 23 down
+// columns stored.
+constexpr int STAMPS = 24;
 constexpr size_t CTRL_BYTES = 256;
 
 // Global scratch of one step launch (byte offsets, each 256-byte aligned).

@@ -217,13 +217,16 @@ int bread_stack_launches_per_step(const bread_stack_t *st, int T);
  * kernel_ms[4*layer + k], k = 0..3. */
 int bread_stack_profile_step(bread_stack_t *st, float *h, int T, cudaStream_t stream, float *kernel_ms);
 /* Raw timestamps (ns, %globaltimer) of the last profiled step:
- * out[(layer * ctas + cta) * 16 + k].  Consumer points k = 0 layer start,
+ * out[(layer * ctas + cta) * 24 + k].  Consumer points k = 0 layer start,
  * 1 logits written, 2 after the router barrier, 3 routing tables built,
  * 4 first activation slot landed, 5 gate/up done, 6 after the gate/up
  * barrier, 7 first down stage landed, 8 down done, 9 layer end; producer
  * points 10 routing tables seen, 11 gate/up copies issued, 12 down weight
  * copies issued, 13 next router rows issued, 14 gate/up barrier seen, 15 all
- * down copies issued.  *ctas receives the grid size.  Synchronous. */
+ * down copies issued; consumer again 16 quantisation share done, 17 router
+ * rows landed, 18 router dots done, 19 routing inputs read, 20 top-k done,
+ * 21 tables built, 22 down stages done, 23 down columns stored.  *ctas
+ * receives the grid size.  Synchronous. */
 int bread_stack_profile_stamps(const bread_stack_t *st, unsigned long long *out, size_t n_words, int *ctas);
 /* Per layer of the last step: expert groups computed here (distinct routed
  * experts + the shared expert) and (token, expert) pairs.  Synchronous. */
