@@ -51,6 +51,8 @@ constexpr int BAR_ALL = 2;       // consumers + producer: routing tables ready
 constexpr size_t SMEM_LIMIT = 232448;  // dynamic shared memory per CTA (227 KB)
 constexpr unsigned long long GRID_WAIT_NS = 2000000000ull;  // 2 s
 constexpr unsigned long long EP_WAIT_NS = 20000000000ull;   // 20 s (peers may start late)
+constexpr int ROUTE_DIST_T = 16;  // above this many tokens the grid routes them (one warp each)
+constexpr int ROUTER_TILE_T = 8;  // above this many tokens the router works in 16-row x 8-token units
 
 template <int NBH, int NBI>
 struct SCfg {
@@ -247,84 +249,112 @@ __device__ __forceinline__ ChunkInfo chunk_search(const RouteTabs &R, int c)
 // then the (token, expert) pairs grouped by expert: group 0 is the shared
 // expert (all T tokens), then the routed experts held here by ascending id,
 // pairs token-major inside each group.
+// Routes token t (one warp): RMS factor from the group sums of squares, top-k
+// of the scaled logits (see below), renormalised weights, the shared gate's
+// sigmoid (0.5 without a gate vector, one_layer.cu:944,1889).  Writes
+// idx/w [t*K + k], rinv/sgw [t]; `outputs` also writes the caller's copies.
+template <int PER>
+__device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *idx, float *w, float *rinv,
+                            float *sgw, bool outputs, unsigned long long *st)
+{
+    const int lane = threadIdx.x & 31;
+    const int H = a.H, E = a.E, K = a.top_k, HG = H / 32;
+    float p[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int e = lane + 32 * j;
+        p[j] = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
+    }
+    float ss = 0.0f;
+    for (int g = lane; g < HG; g += 32) ss += __ldcg(a.ssq + t * HG + g);
+    const float score = Ld.w_sg ? __ldcg(a.score + t) : 0.0f;
+    ss = warp_sum(ss);
+    const float r = a.norm_eps >= 0.0f ? rsqrtf(ss / (float)H + a.norm_eps) : 1.0f;
+    if (st) st[19] = globaltimer();
+    // top-k by repeated argmax over the RMS-scaled logits.  The softmax is
+    // monotonic, so this selects what cpu_topk selects on the probabilities
+    // (strict >: the lowest index wins ties); and the renormalised weights
+    // p_k / sum(p_top) = exp(l_k - l_max) / sum exp(l_top - l_max) need no
+    // full softmax.  Keys: the float bits made order-preserving as unsigned
+    // (0 = taken or no expert); one warp max finds the value, one warp min the
+    // lowest index holding it.
+    unsigned key[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const unsigned b = __float_as_uint(p[j] * r);
+        key[j] = (lane + 32 * j) < E ? (b & 0x80000000u ? ~b : b | 0x80000000u) : 0u;
+    }
+    float my_l = 0.0f, lmax = 0.0f;
+    int my_i = 0;
+    for (int k = 0; k < K; ++k) {
+        unsigned best = 0;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) best = key[j] > best ? key[j] : best;
+        const unsigned mk = __reduce_max_sync(0xffffffffu, best);
+        unsigned cand = 0xffffffffu;
+#pragma unroll
+        for (int j = PER - 1; j >= 0; --j)
+            if (key[j] == mk) cand = (unsigned)(lane + 32 * j);
+        const unsigned bi = __reduce_min_sync(0xffffffffu, cand);
+        if ((int)(bi & 31) == lane) {
+#pragma unroll
+            for (int j = 0; j < PER; ++j)
+                if (j == (int)(bi >> 5)) key[j] = 0;
+        }
+        const float lv = __uint_as_float(mk & 0x80000000u ? mk & 0x7fffffffu : ~mk);
+        if (k == 0) lmax = lv;
+        if (lane == k) {
+            my_l = lv;
+            my_i = (int)bi;
+        }
+    }
+    const float my_e = lane < K ? expf(my_l - lmax) : 0.0f;
+    const float wsum = warp_sum(my_e);
+    const float my_w = my_e / wsum;
+    if (st) st[20] = globaltimer();
+    if (lane < K) {
+        idx[t * K + lane] = my_i;
+        w[t * K + lane] = my_w;
+        if (outputs && a.idx_out) a.idx_out[t * K + lane] = my_i;
+        if (outputs && a.w_out) a.w_out[t * K + lane] = my_w;
+    }
+    if (lane == 0) {
+        const float sg = Ld.w_sg ? 1.0f / (1.0f + expf(-(score * r))) : 0.5f;
+        rinv[t] = r;
+        sgw[t] = sg;
+        if (outputs && a.sg_out) a.sg_out[t] = sg;
+    }
+}
+
+// Phase B routing tables, run by the 256 consumer threads of every CTA.
+// Local (dist = false): the CTA routes every token itself.  Distributed: the
+// grid routed the tokens into global memory (route_token, then a grid
+// barrier) and the CTA copies them.  Then the (token, expert) pairs are
+// grouped by expert: group 0 is the shared expert (all T tokens), then the
+// routed experts held here, pairs token-major inside each group.
 template <int PER>
 __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const RouteTabs &R, int l, bool cta0,
-                             unsigned long long *st)
+                             unsigned long long *st, bool dist)
 {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int T = a.T, H = a.H, E = a.E, K = a.top_k, HG = H / 32;
+    const int T = a.T, E = a.E, K = a.top_k;
     const int EL = a.hi - a.lo;
     for (int i = tid; i < EL; i += ST_CONS) {
         R.cnt[i] = 0;
         R.run[i] = 0;
     }
-    for (int t = warp; t < T; t += 8) {
-        float p[PER];
-#pragma unroll
-        for (int j = 0; j < PER; ++j) {
-            const int e = lane + 32 * j;
-            p[j] = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
+    if (dist) {
+        for (int i = tid; i < T * K; i += ST_CONS) {
+            R.idx[i] = __ldcg(a.ridx + i);
+            R.w[i] = __ldcg(a.rw + i);
         }
-        float ss = 0.0f;
-        for (int g = lane; g < HG; g += 32) ss += __ldcg(a.ssq + t * HG + g);
-        const float score = Ld.w_sg ? __ldcg(a.score + t) : 0.0f;
-        ss = warp_sum(ss);
-        const float r = a.norm_eps >= 0.0f ? rsqrtf(ss / (float)H + a.norm_eps) : 1.0f;
-        if (st && tid == 0) st[19] = globaltimer();
-        // top-k by repeated argmax over the RMS-scaled logits.  The softmax is
-        // monotonic, so this selects what cpu_topk selects on the
-        // probabilities (strict >: the lowest index wins ties); and the
-        // renormalised weights p_k / sum(p_top) = exp(l_k - l_max) / sum
-        // exp(l_top - l_max) need no full softmax.  Keys: the float bits made
-        // order-preserving as unsigned (0 = taken or no expert); one warp max
-        // finds the value, one warp min the lowest index holding it.
-        unsigned key[PER];
-#pragma unroll
-        for (int j = 0; j < PER; ++j) {
-            const unsigned b = __float_as_uint(p[j] * r);
-            key[j] = (lane + 32 * j) < E ? (b & 0x80000000u ? ~b : b | 0x80000000u) : 0u;
+        for (int i = tid; i < T; i += ST_CONS) {
+            R.rinv[i] = __ldcg(a.rinv + i);
+            R.sgw[i] = __ldcg(a.rsgw + i);
         }
-        float my_l = 0.0f, lmax = 0.0f;
-        int my_i = 0;
-        for (int k = 0; k < K; ++k) {
-            unsigned best = 0;
-#pragma unroll
-            for (int j = 0; j < PER; ++j) best = key[j] > best ? key[j] : best;
-            const unsigned mk = __reduce_max_sync(0xffffffffu, best);
-            unsigned cand = 0xffffffffu;
-#pragma unroll
-            for (int j = PER - 1; j >= 0; --j)
-                if (key[j] == mk) cand = (unsigned)(lane + 32 * j);
-            const unsigned bi = __reduce_min_sync(0xffffffffu, cand);
-            if ((int)(bi & 31) == lane) {
-#pragma unroll
-                for (int j = 0; j < PER; ++j)
-                    if (j == (int)(bi >> 5)) key[j] = 0;
-            }
-            const float lv = __uint_as_float(mk & 0x80000000u ? mk & 0x7fffffffu : ~mk);
-            if (k == 0) lmax = lv;
-            if (lane == k) {
-                my_l = lv;
-                my_i = (int)bi;
-            }
-        }
-        const float my_e = lane < K ? expf(my_l - lmax) : 0.0f;
-        const float wsum = warp_sum(my_e);
-        const float my_w = my_e / wsum;
-        if (st && tid == 0) st[20] = globaltimer();
-        if (lane < K) {
-            const float w = my_w;
-            R.idx[t * K + lane] = my_i;
-            R.w[t * K + lane] = w;
-            if (cta0 && a.idx_out) a.idx_out[t * K + lane] = my_i;
-            if (cta0 && a.w_out) a.w_out[t * K + lane] = w;
-        }
-        if (lane == 0) {
-            const float sg = Ld.w_sg ? 1.0f / (1.0f + expf(-(score * r))) : 0.5f;
-            R.rinv[t] = r;
-            R.sgw[t] = sg;
-            if (cta0 && a.sg_out) a.sg_out[t] = sg;
-        }
+    } else {
+        for (int t = warp; t < T; t += 8)
+            route_token<PER>(a, Ld, t, R.idx, R.w, R.rinv, R.sgw, cta0, (st && tid == 0) ? st : nullptr);
     }
     named_sync(BAR_CONS, ST_CONS);
     if (a.route_only) return;
@@ -553,6 +583,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
     const bool ep = a.ep_world > 1;
     const bool norm = a.norm_eps >= 0.0f;
     const int NS_G = m.NS_G, NS_D = m.NS_D;
+    const bool dist = T > ROUTE_DIST_T;               // routing spread over the grid (+1 barrier)
+    const int nbl = (ep ? 2 : 3) + (dist ? 1 : 0);    // grid barriers per layer
 
     float *rbuf = reinterpret_cast<float *>(smem + m.rbuf);
     float *part = reinterpret_cast<float *>(smem + m.part);
@@ -619,6 +651,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         // Router rows of layer l (and the shared-gate vector as row E) -> rbuf.
         auto issue_router = [&](int l) {
             const StepLayer Ld = layer_desc(a, l);
+            if (T > ROUTER_TILE_T) {
+                // tiled router: warm L2 with the rows of this CTA's units
+                const int nrows = E + (Ld.w_sg ? 1 : 0);
+                const int nrb = (nrows + 15) / 16;
+                for (int u = bx + G * lane; u < nrb * ((T + 7) / 8); u += G * 32) {
+                    const int r0 = (u % nrb) * 16, r1 = r0 + 16 < E ? r0 + 16 : E;
+                    if (r1 > r0) prefetch_l2(Ld.W_r + (size_t)r0 * H, (unsigned)((r1 - r0) * H * 4));
+                }
+                if (lane == 0) mbar_arrive(rbar);
+                return;
+            }
             unsigned bytes = 0;
             for (int rl = 0; rl < m.RR; ++rl) {
                 const int r = bx * m.RR + rl;
@@ -743,7 +786,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             pstamp(l, 13);
             // the intermediate of every CTA is complete after grid barrier (phase B)
             if (lane == 0) {
-                const int bidx = ep ? 2 * l + 1 : 3 * l + 1;
+                const int bidx = l * nbl + (dist ? 2 : 1);
                 wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(bidx + 1) * G, false, GRID_WAIT_NS);
             }
             __syncwarp();
@@ -827,7 +870,70 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         // (3) router rows of this CTA (row E = fp16 shared-gate vector)
         swait(rbar, (unsigned)(l & 1));
         if (stamp) stamp_at(l, 17);
-        {
+        if (T > ROUTER_TILE_T) {
+            // Many tokens: units of 16 router rows x 8 tokens.  The unit's
+            // tokens are staged in shared memory (the activation slots are idle
+            // in this phase); each warp computes two whole rows for them, with
+            // the rows read from L2 (prefetched during the previous layer).
+            const int nrows = E + (Ld.w_sg ? 1 : 0);
+            const int nrb = (nrows + 15) / 16, ntb = (T + 7) / 8;
+            float *xst = reinterpret_cast<float *>(xsl);
+            for (int u = bx; u < nrb * ntb; u += G) {
+                const int rb = u % nrb, t0 = (u / nrb) * 8;
+                const int tn = T - t0 < 8 ? T - t0 : 8;
+                for (int i = tid; i < tn * (H / 4); i += ST_CONS) {
+                    const int t = i / (H / 4), c4 = i % (H / 4);
+                    reinterpret_cast<float4 *>(xst)[i] = xin4((size_t)(t0 + t) * H + 4 * c4);
+                }
+                named_sync(BAR_CONS, ST_CONS);
+                for (int rr = 0; rr < 2; ++rr) {
+                    const int row = rb * 16 + 2 * warp + rr;
+                    if (row >= nrows) break;
+                    float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                    for (int cb = 0; cb < H; cb += 512) {
+                        float4 w4[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const int c = cb + 4 * lane + 128 * j;
+                            if (row < E) {
+                                w4[j] = __ldcg(reinterpret_cast<const float4 *>(Ld.W_r + (size_t)row * H + c));
+                            } else {
+                                const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(Ld.w_sg + c));
+                                const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(Ld.w_sg + c + 2));
+                                w4[j] = make_float4(lo.x, lo.y, hi.x, hi.y);
+                            }
+                        }
+#pragma unroll
+                        for (int t = 0; t < 8; ++t)
+                            if (t < tn) {
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    const float4 x4 =
+                                        reinterpret_cast<const float4 *>(xst)[((size_t)t * H + cb + 4 * lane + 128 * j) >> 2];
+                                    acc8[t] = fmaf(w4[j].x, x4.x,
+                                                   fmaf(w4[j].y, x4.y, fmaf(w4[j].z, x4.z, fmaf(w4[j].w, x4.w, acc8[t]))));
+                                }
+                            }
+                    }
+#pragma unroll
+                    for (int t = 0; t < 8; ++t)
+                        if (t < tn) {
+                            const float v = warp_sum(acc8[t]);
+                            if (lane == 0) {
+                                if (row < E)
+                                    a.logits[(size_t)(t0 + t) * E + row] = v;
+                                else
+                                    a.score[t0 + t] = v;
+                            }
+                        }
+                }
+                // the staging area is refilled next (generic writes) and later by
+                // bulk copies (async proxy)
+                fence_proxy_async_smem();
+                named_sync(BAR_CONS, ST_CONS);
+            }
+            if (stamp) stamp_at(l, 18);
+        } else {
             const int rl = warp / m.WPR, qt = warp % m.WPR;
             const int row = bx * m.RR + rl;
             const int nrows = E + (Ld.w_sg ? 1 : 0);
@@ -908,10 +1014,20 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
 
         // ------------------------------------------------------------ phase B
         unsigned long long *st_l = stamp ? a.stamps + ((size_t)l * G + bx) * STAMPS : nullptr;
+        if (dist) {
+            // one warp of the grid per token, then every CTA reads the result
+            for (int t = bx * 8 + warp; t < T; t += G * 8) {
+                if (E <= 256)
+                    route_token<8>(a, Ld, t, a.ridx, a.rw, a.rinv, a.rsgw, true, nullptr);
+                else
+                    route_token<MOE_EMAX / 32>(a, Ld, t, a.ridx, a.rw, a.rinv, a.rsgw, true, nullptr);
+            }
+            grid_barrier(a, bar++, tid);
+        }
         if (E <= 256)
-            route_tables<8>(a, Ld, RT, l, bx == 0, st_l);
+            route_tables<8>(a, Ld, RT, l, bx == 0, st_l, dist);
         else
-            route_tables<MOE_EMAX / 32>(a, Ld, RT, l, bx == 0, st_l);
+            route_tables<MOE_EMAX / 32>(a, Ld, RT, l, bx == 0, st_l, dist);
         if (stamp) stamp_at(l, 3);
         named_sync(BAR_ALL, ST_THREADS);
         if (a.route_only) break;
@@ -1053,10 +1169,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 }
                 if (stamp) stamp_at(l, 23);
                 if (ep) {
-                    __threadfence_system();
+                    // one system-scope release by thread 0, after the CTA barrier
+                    // that orders every thread's partial stores before it
                     named_sync(BAR_CONS, ST_CONS);
-                    if (tid == 0)
-                        for (int p = 0; p < a.ep_world; ++p) atomicAdd_system(ep_counter(a, p, slot_l), 1ull);
+                    if (tid == 0) {
+                        __threadfence_system();
+                        for (int p = 0; p < a.ep_world; ++p) red_release_sys(ep_counter(a, p, slot_l), 1ull);
+                    }
                 }
                 named_sync(BAR_CONS, ST_CONS);
             }
@@ -1266,6 +1385,10 @@ void step_bind_workspace(StepArgs &a, void *ws, const StepWs &L)
     a.xs = reinterpret_cast<float *>(b + L.xs);
     a.aq = reinterpret_cast<int16_t *>(b + L.aq);
     a.as = reinterpret_cast<float *>(b + L.as);
+    a.ridx = reinterpret_cast<int *>(b + L.ridx);
+    a.rw = reinterpret_cast<float *>(b + L.rw);
+    a.rinv = reinterpret_cast<float *>(b + L.rinv);
+    a.rsgw = reinterpret_cast<float *>(b + L.rsgw);
     a.buf[0] = L.buf0 ? reinterpret_cast<float *>(b + L.buf0) : nullptr;
     a.buf[1] = L.buf1 ? reinterpret_cast<float *>(b + L.buf1) : nullptr;
 }

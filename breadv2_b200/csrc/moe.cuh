@@ -70,7 +70,7 @@ constexpr size_t CTRL_BYTES = 256;
 
 // Global scratch of one step launch (byte offsets, each 256-byte aligned).
 struct StepWs {
-    size_t ctrl, logits, score, ssq, xq, xs, aq, as, buf0, buf1, total;
+    size_t ctrl, logits, score, ssq, xq, xs, aq, as, ridx, rw, rinv, rsgw, buf0, buf1, total;
     int PM;
     __host__ static StepWs make(int T, int H, int I, int E, int K, bool inter_layer_buffers)
     {
@@ -90,6 +90,10 @@ struct StepWs {
         w.xs = take((size_t)T * (H / 32) * 4);
         w.aq = take((size_t)w.PM * (I > 0 ? I : 32) * 2);
         w.as = take((size_t)w.PM * (I > 0 ? I / 32 : 1) * 4);
+        w.ridx = take((size_t)T * K * 4);
+        w.rw = take((size_t)T * K * 4);
+        w.rinv = take((size_t)T * 4);
+        w.rsgw = take((size_t)T * 4);
         w.buf0 = inter_layer_buffers ? take((size_t)T * H * 4) : 0;
         w.buf1 = inter_layer_buffers ? take((size_t)T * H * 4) : 0;
         w.total = o;
@@ -144,6 +148,8 @@ struct StepArgs {
     float *xs;
     int16_t *aq;
     float *as;
+    int *ridx;                  // routing of the grid (large T): [T x k] experts and weights,
+    float *rw, *rinv, *rsgw;    // [T] RMS factors and shared-gate weights
     // optional outputs (written by CTA 0)
     int *idx_out;
     float *w_out, *sg_out;

@@ -73,6 +73,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// Prefetch [src, src + bytes) into L2 (bulk, no destination).  src 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 // Order this thread's generic-proxy shared-memory accesses before later
 // async-proxy (bulk copy) accesses of the same bytes.
 __device__ __forceinline__ void fence_proxy_async_smem()
@@ -100,6 +106,11 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     unsigned long long v;
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+// Release-add at system scope (arrival counters in peers' memory over NVLink).
+__device__ __forceinline__ void red_release_sys(unsigned long long *p, unsigned long long v)
+{
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ unsigned long long globaltimer()
 {
