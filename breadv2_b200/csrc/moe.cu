@@ -584,6 +584,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
     const bool norm = a.norm_eps >= 0.0f;
     const int NS_G = m.NS_G, NS_D = m.NS_D;
     const bool dist = T > ROUTE_DIST_T;               // routing spread over the grid (+1 barrier)
+    const bool arena = T > ROUTER_TILE_T;             // gate/up and down rings share shared memory
     const int nbl = (ep ? 2 : 3) + (dist ? 1 : 0);    // grid barriers per layer
 
     float *rbuf = reinterpret_cast<float *>(smem + m.rbuf);
@@ -702,7 +703,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         // copy its first sub-stages at the next ring positions (ring drained).
         auto preissue_shared = [&](int l) -> int {
             const StepLayer Ld = layer_desc(a, l);
-            if (a.route_only || !Ld.sh_gate || bx >= ((T + MOE_TC - 1) / MOE_TC) * R) return 0;
+            if (arena || a.route_only || !Ld.sh_gate || bx >= ((T + MOE_TC - 1) / MOE_TC) * R) return 0;
             const int npre = C::SPI < NS_G ? C::SPI : NS_G;
             if (lane < npre)
                 issue_gu(gR.ahead(lane, NS_G), Ld.sh_gate, Ld.sh_up,
@@ -756,7 +757,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             // the grid barrier
             const int my_tiles = bx < NT ? (NT - 1 - bx) / G + 1 : 0;
             const int nds = my_tiles * nch;
-            const int dpre = nds < NS_D ? nds : NS_D;
+            const int dpre = arena ? 0 : (nds < NS_D ? nds : NS_D);
             auto issue_dw = [&](const Ring &d, int n) {
                 if (d.used) swait(dempty + d.slot, (unsigned)(d.phase ^ 1));
                 const ChunkInfo ci = chunk_info(RT, n % nch);
@@ -890,12 +891,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     const int row = rb * 16 + 2 * warp + rr;
                     if (row >= nrows) break;
                     float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                    for (int cb = 0; cb < H; cb += 512) {
-                        float4 w4[4];
+                    for (int cb = 0; cb < H; cb += 1024) {  // 8 loads per lane in flight per round
+                        float4 w4[8];
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
+                        for (int j = 0; j < 8; ++j) {
                             const int c = cb + 4 * lane + 128 * j;
-                            if (row < E) {
+                            if (c >= H) {
+                                w4[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            } else if (row < E) {
                                 w4[j] = __ldcg(reinterpret_cast<const float4 *>(Ld.W_r + (size_t)row * H + c));
                             } else {
                                 const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(Ld.w_sg + c));
@@ -907,11 +910,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                         for (int t = 0; t < 8; ++t)
                             if (t < tn) {
 #pragma unroll
-                                for (int j = 0; j < 4; ++j) {
-                                    const float4 x4 =
-                                        reinterpret_cast<const float4 *>(xst)[((size_t)t * H + cb + 4 * lane + 128 * j) >> 2];
-                                    acc8[t] = fmaf(w4[j].x, x4.x,
-                                                   fmaf(w4[j].y, x4.y, fmaf(w4[j].z, x4.z, fmaf(w4[j].w, x4.w, acc8[t]))));
+                                for (int j = 0; j < 8; ++j) {
+                                    const int c = cb + 4 * lane + 128 * j;
+                                    if (c < H) {
+                                        const float4 x4 = reinterpret_cast<const float4 *>(xst)[((size_t)t * H + c) >> 2];
+                                        acc8[t] = fmaf(w4[j].x, x4.x,
+                                                       fmaf(w4[j].y, x4.y, fmaf(w4[j].z, x4.z, fmaf(w4[j].w, x4.w, acc8[t]))));
+                                    }
                                 }
                             }
                     }
@@ -1087,6 +1092,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             }
         }
         if (stamp) stamp_at(l, 5);
+        if (arena) fence_proxy_async_smem();  // the down copies reuse the gate/up stages' bytes
         grid_barrier(a, bar++, tid);
         if (stamp) stamp_at(l, 6);
 
@@ -1098,6 +1104,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             const int rho = lane / GI::LPR, lr = lane % GI::LPR, bb = lr >> 2, sub = lr & 3;
             const Q6Lane L6 = q6_lane(((rho * NBI + bb) & 1) ? 2 : 0, sub & 1);
             float *my_acc = acc + (size_t)warp * T * MOE_RT3;
+            // Work units: a chunk's 16 rows (WS warp steps), or half of them
+            // when the chunks are too few to keep the 8 warps busy.  A unit's
+            // warp loads each token's activation slice once and runs the
+            // unit's row dot products from it (independent chains).
+            const int WG = (nch >= 8 || C::WS < 2) ? C::WS : C::WS / 2;
+            const int UPC = C::WS / WG;
             for (int it3 = bx; it3 < NT; it3 += G) {
                 // residual of this tile's columns, loaded before the stages
                 float rv[MOE_TMAX * MOE_RT3 / ST_CONS];
@@ -1108,43 +1120,55 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                                 ? __ldcg(res + (size_t)(i / MOE_RT3) * H + (size_t)it3 * MOE_RT3 + i % MOE_RT3)
                                 : 0.0f;
                 }
-                for (int c = 0; c < nch; ++c, dR.next(NS_D)) {
-                    const int slot = dR.slot;
-                    const unsigned par = (unsigned)dR.phase;
+                // Rounds of RSU units whose chunks sit in distinct ring slots, with
+                // a consumer barrier between rounds: a slot's previous use is then
+                // finished before any warp waits on it again, so the parity wait
+                // below never looks two phases ahead.
+                const int RSU = 8 < NS_D * UPC ? 8 : NS_D * UPC;
+                for (int r0 = 0; r0 < nch * UPC; r0 += RSU) {
+                    const int u = r0 + warp;
+                    if (warp >= RSU || u >= nch * UPC) {
+                        named_sync(BAR_CONS, ST_CONS);
+                        continue;
+                    }
+                    const int c = u / UPC, ws0 = (u - c * UPC) * WG;
+                    const int pos = dR.slot + c;  // ring position of chunk c from the tile's first stage
+                    const int slot = pos % NS_D;
+                    const unsigned par = (unsigned)(dR.phase ^ ((pos / NS_D) & 1));
                     const uint8_t *st = dring + (size_t)slot * m.dslot;
-                    bool waited = false;
-                    ChunkInfo ci{0, 0, 0};
-                    for (int ws = 0; ws < C::WS; ++ws) {
-                        if (((c * C::WS + ws) & 7) != warp) continue;
-                        if (!waited) {
-                            swait(dw + slot, par);
-                            swait(da + slot, par);
-                            if (stamp && c == 0 && it3 == bx) stamp_at(l, 7);
-                            ci = chunk_info(RT, c);
-                            waited = true;
-                        }
-                        const uint8_t *rowp = st + (size_t)ws * GI::STEPB + (size_t)rho * GI::ROWB;
-                        const int16_t *aqs = reinterpret_cast<const int16_t *>(st + C::WB);
-                        const float *ass = reinterpret_cast<const float *>(st + C::WB + (size_t)TC * I * 2);
-                        for (int j = 0; j < ci.np; ++j) {
-                            const int t = RT.ptok[ci.p0 + j];
-                            const float wgt = RT.pw[ci.p0 + j];
+                    swait(dw + slot, par);
+                    swait(da + slot, par);
+                    if (stamp && r0 == 0 && it3 == bx) stamp_at(l, 7);
+                    const ChunkInfo ci = chunk_info(RT, c);
+                    const int16_t *aqs = reinterpret_cast<const int16_t *>(st + C::WB);
+                    const float *ass = reinterpret_cast<const float *>(st + C::WB + (size_t)TC * I * 2);
+                    for (int j = 0; j < ci.np; ++j) {
+                        const int t = RT.ptok[ci.p0 + j];
+                        const float wgt = RT.pw[ci.p0 + j];
+                        XSlice X[GI::CP];
+#pragma unroll
+                        for (int cp = 0; cp < GI::CP; ++cp)
+                            load_slice_q6k(X[cp], aqs + (size_t)j * I, ass + (size_t)j * (I / 32),
+                                           QK * (cp * 8 + bb) + 128 * (sub >> 1), sub & 1);
+#pragma unroll
+                        for (int wi = 0; wi < C::WS; ++wi) {
+                            if (wi >= WG) continue;
+                            const int ws = ws0 + wi;
+                            const uint8_t *rowp = st + (size_t)ws * GI::STEPB + (size_t)rho * GI::ROWB;
                             float v = 0.0f;
 #pragma unroll
-                            for (int cp = 0; cp < GI::CP; ++cp) {
-                                XSlice X;
-                                load_slice_q6k(X, aqs + (size_t)j * I, ass + (size_t)j * (I / 32),
-                                               QK * (cp * 8 + bb) + 128 * (sub >> 1), sub & 1);
-                                v += q6k_lane_dot(rowp + (size_t)(cp * 8 + bb) * Q6K_BYTES, sub >> 1, sub & 1, L6, X);
-                            }
+                            for (int cp = 0; cp < GI::CP; ++cp)
+                                v += q6k_lane_dot(rowp + (size_t)(cp * 8 + bb) * Q6K_BYTES, sub >> 1, sub & 1, L6, X[cp]);
 #pragma unroll
                             for (int o = GI::LPR / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                             if (lr == 0) my_acc[t * MOE_RT3 + ws * GI::RPW + rho] += wgt * v;
                         }
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(dempty + slot);
                     }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cnt(dempty + slot, (unsigned)WG);
+                    named_sync(BAR_CONS, ST_CONS);
                 }
+                for (int c = 0; c < nch; ++c) dR.next(NS_D);
                 if (stamp) stamp_at(l, 22);
                 named_sync(BAR_CONS, ST_CONS);
 #pragma unroll
@@ -1154,7 +1178,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     const int t = i / MOE_RT3, r = i % MOE_RT3;
                     float s = 0.0f;
 #pragma unroll
-                    for (int w = 0; w < 8; ++w) {
+                    for (int w = 0; w < 8; ++w) {  // warps in order: a fixed summation order
                         s += acc[(size_t)w * T * MOE_RT3 + i];
                         acc[(size_t)w * T * MOE_RT3 + i] = 0.0f;
                     }
@@ -1181,6 +1205,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             }
         }
         if (stamp) stamp_at(l, 8);
+        if (arena) fence_proxy_async_smem();  // the next gate/up copies reuse the down stages' bytes
         if (!ep) grid_barrier(a, bar++, tid);
         if (stamp) stamp_at(l, 9);
     }
@@ -1236,7 +1261,8 @@ static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G)
     if (rr > 8) return -1;
     m.RR = rr;
     m.WPR = 8 / rr;
-    m.rbuf = take((size_t)rr * C::H * 4, 128);
+    const bool arena = T > ROUTER_TILE_T;  // tiled router (no rows in smem), rings share one arena
+    m.rbuf = take(arena ? 16 : (size_t)rr * C::H * 4, 128);
     m.part = take((size_t)8 * T * 4, 16);
     const int GM = (EL < T * K ? EL : T * K) + 1, PM = T * (K + 1);
     m.r_idx = take((size_t)T * K * 4, 16);
@@ -1258,22 +1284,38 @@ static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G)
     const int TC = T < MOE_TC ? T : MOE_TC;
     m.xslot = (uint32_t)al16((size_t)TC * C::XTOK);
     m.xsl = take(2 * (size_t)m.xslot, 128);
-    int nsg = 4;
-    while (nsg > 2 && (size_t)nsg * C::STB > 80 * 1024) --nsg;
-    if (T > MOE_TC) nsg = 2;
-    m.NS_G = nsg;
-    m.gring = take((size_t)nsg * C::STB, 128);
     m.abuf = take((size_t)TC * MOE_ROWTILE * 4, 16);
     m.acc = take((size_t)8 * T * MOE_RT3 * 4, 16);
     m.dslot = (uint32_t)al16((size_t)C::WB + (size_t)TC * C::ATOK);
-    const size_t bars_max = (size_t)(1 + 2 * nsg + 4 + 3 * 16) * 8 + 8;
-    const size_t d0 = (o + 127) / 128 * 128;
-    const size_t avail = SMEM_LIMIT > d0 + bars_max ? SMEM_LIMIT - d0 - bars_max : 0;
-    int nsd = (int)(avail / m.dslot);
-    if (nsd > 16) nsd = 16;
-    if (nsd < 2) return -1;
+    const size_t bars_max = (size_t)(1 + 2 * 16 + 4 + 3 * 16) * 8 + 8;
+    int nsg, nsd;
+    if (!arena) {
+        // few tokens: separate rings, so the down weights can be in flight
+        // during the gate/up phase
+        nsg = 4;
+        while (nsg > 2 && (size_t)nsg * C::STB > 80 * 1024) --nsg;
+        m.gring = take((size_t)nsg * C::STB, 128);
+        const size_t d0 = (o + 127) / 128 * 128;
+        const size_t avail = SMEM_LIMIT > d0 + bars_max ? SMEM_LIMIT - d0 - bars_max : 0;
+        nsd = (int)(avail / m.dslot);
+        if (nsd > 16) nsd = 16;
+        m.dring = take((size_t)(nsd > 0 ? nsd : 0) * m.dslot, 128);
+    } else {
+        // many tokens: both rings in one arena (the down phase starts after
+        // every gate/up stage of the CTA is consumed), as deep as it allows
+        const size_t a0 = (o + 127) / 128 * 128;
+        const size_t avail = SMEM_LIMIT > a0 + bars_max ? SMEM_LIMIT - a0 - bars_max : 0;
+        nsg = (int)(avail / C::STB);
+        nsd = (int)(avail / m.dslot);
+        if (nsg > 16) nsg = 16;
+        if (nsd > 16) nsd = 16;
+        m.gring = m.dring = (uint32_t)a0;
+        const size_t gb = (size_t)(nsg > 0 ? nsg : 0) * C::STB, db = (size_t)(nsd > 0 ? nsd : 0) * m.dslot;
+        o = a0 + (gb > db ? gb : db);
+    }
+    if (nsg < 2 || nsd < 2) return -1;
+    m.NS_G = nsg;
     m.NS_D = nsd;
-    m.dring = take((size_t)nsd * m.dslot, 128);
     m.bars = take((size_t)(1 + 2 * nsg + 4 + 3 * nsd) * 8, 8);
     m.total = (uint32_t)o;
     return o <= SMEM_LIMIT ? 0 : -1;
