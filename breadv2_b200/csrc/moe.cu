@@ -1051,13 +1051,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 const uint8_t *xb = xsl + (size_t)xs_ * m.xslot;
                 const int16_t *xq = reinterpret_cast<const int16_t *>(xb);
                 const float *xsc = reinterpret_cast<const float *>(xb + (size_t)TC * H * 2);
-                for (int s = 0; s < C::SPI; ++s, gR.next(NS_G)) {
-                    const int slot = gR.slot;
-                    swait(gfull + slot, (unsigned)gR.phase);
-                    const uint8_t *grow = gring + (size_t)slot * C::STB + (size_t)rs * GH::ROWB;
-                    const uint8_t *urow = grow + (size_t)C::SR * GH::ROWB;
+                if (C::SPI <= NS_G) {
+                    // The item's sub-stages are in flight together: wait for all,
+                    // then per token one activation slice feeds the item's
+                    // 2 x SPI row dot products (independent chains).
+#pragma unroll
+                    for (int s = 0; s < C::SPI; ++s) {
+                        const Ring g = gR.ahead(s, NS_G);
+                        swait(gfull + g.slot, (unsigned)g.phase);
+                    }
                     for (int j = 0; has_rows && j < ci.np; ++j) {
-                        if (ci.np > 1 || s == 0) {  // one token: its slice stays in registers across sub-stages
+                        if (ci.np > 1 || j == 0) {
                             const int t = RT.ptok[ci.p0 + j];
                             const float rsc = norm ? RT.rinv[t] : 1.0f;
 #pragma unroll
@@ -1065,21 +1069,68 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                                 load_slice_q4k(X[cp], xq + (size_t)j * H, xsc + (size_t)j * (H / 32),
                                                QK * (cp * 8 + bb) + 64 * sub, rsc);
                         }
-                        float gs = 0.0f, us = 0.0f;
+                        float gs[C::SPI], us[C::SPI];
 #pragma unroll
-                        for (int cp = 0; cp < GH::CP; ++cp) {
-                            gs += q4k_lane_dot(grow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
-                            us += q4k_lane_dot(urow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                        for (int s = 0; s < C::SPI; ++s) {
+                            const uint8_t *grow =
+                                gring + (size_t)gR.ahead(s, NS_G).slot * C::STB + (size_t)rs * GH::ROWB;
+                            const uint8_t *urow = grow + (size_t)C::SR * GH::ROWB;
+                            gs[s] = 0.0f;
+                            us[s] = 0.0f;
+#pragma unroll
+                            for (int cp = 0; cp < GH::CP; ++cp) {
+                                gs[s] += q4k_lane_dot(grow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                                us[s] += q4k_lane_dot(urow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                            }
                         }
 #pragma unroll
-                        for (int o = GH::LPR / 2; o; o >>= 1) {
-                            gs += __shfl_xor_sync(0xffffffffu, gs, o);
-                            us += __shfl_xor_sync(0xffffffffu, us, o);
-                        }
-                        if (lr == 0) abuf[j * MOE_ROWTILE + s * C::SR + rs] = gs / (1.0f + expf(-gs)) * us;
+                        for (int o = GH::LPR / 2; o; o >>= 1)
+#pragma unroll
+                            for (int s = 0; s < C::SPI; ++s) {
+                                gs[s] += __shfl_xor_sync(0xffffffffu, gs[s], o);
+                                us[s] += __shfl_xor_sync(0xffffffffu, us[s], o);
+                            }
+                        if (lr == 0)
+#pragma unroll
+                            for (int s = 0; s < C::SPI; ++s)
+                                abuf[j * MOE_ROWTILE + s * C::SR + rs] = gs[s] / (1.0f + expf(-gs[s])) * us[s];
                     }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(gempty + slot);
+                    if (lane == 0)
+#pragma unroll
+                        for (int s = 0; s < C::SPI; ++s) mbar_arrive(gempty + gR.ahead(s, NS_G).slot);
+                    gR = gR.ahead(C::SPI, NS_G);
+                } else {
+                    for (int s = 0; s < C::SPI; ++s, gR.next(NS_G)) {
+                        const int slot = gR.slot;
+                        swait(gfull + slot, (unsigned)gR.phase);
+                        const uint8_t *grow = gring + (size_t)slot * C::STB + (size_t)rs * GH::ROWB;
+                        const uint8_t *urow = grow + (size_t)C::SR * GH::ROWB;
+                        for (int j = 0; has_rows && j < ci.np; ++j) {
+                            if (ci.np > 1 || s == 0) {  // one token: its slice stays in registers across sub-stages
+                                const int t = RT.ptok[ci.p0 + j];
+                                const float rsc = norm ? RT.rinv[t] : 1.0f;
+#pragma unroll
+                                for (int cp = 0; cp < GH::CP; ++cp)
+                                    load_slice_q4k(X[cp], xq + (size_t)j * H, xsc + (size_t)j * (H / 32),
+                                                   QK * (cp * 8 + bb) + 64 * sub, rsc);
+                            }
+                            float gs = 0.0f, us = 0.0f;
+#pragma unroll
+                            for (int cp = 0; cp < GH::CP; ++cp) {
+                                gs += q4k_lane_dot(grow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                                us += q4k_lane_dot(urow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                            }
+#pragma unroll
+                            for (int o = GH::LPR / 2; o; o >>= 1) {
+                                gs += __shfl_xor_sync(0xffffffffu, gs, o);
+                                us += __shfl_xor_sync(0xffffffffu, us, o);
+                            }
+                            if (lr == 0) abuf[j * MOE_ROWTILE + s * C::SR + rs] = gs / (1.0f + expf(-gs)) * us;
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(gempty + slot);
+                    }
                 }
                 named_sync(BAR_CONS, ST_CONS);
                 if (lane == 0) mbar_arrive(xempty + xs_);
