@@ -255,7 +255,8 @@ __device__ __forceinline__ ChunkInfo chunk_search(const RouteTabs &R, int c)
 // idx/w [t*K + k], rinv/sgw [t]; `outputs` also writes the caller's copies.
 template <int PER>
 __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *idx, float *w, float *rinv,
-                            float *sgw, bool outputs, unsigned long long *st)
+                            float *sgw, bool outputs, unsigned long long *st, int *pick_i = nullptr,
+                            float *pick_w = nullptr, float *pick_sg = nullptr)
 {
     const int lane = threadIdx.x & 31;
     const int H = a.H, E = a.E, K = a.top_k, HG = H / 32;
@@ -312,6 +313,11 @@ __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *
     const float wsum = warp_sum(my_e);
     const float my_w = my_e / wsum;
     if (st) st[20] = globaltimer();
+    if (pick_i) {
+        *pick_i = my_i;
+        *pick_w = my_w;
+        *pick_sg = Ld.w_sg ? 1.0f / (1.0f + expf(-(score * r))) : 0.5f;
+    }
     if (lane < K) {
         idx[t * K + lane] = my_i;
         w[t * K + lane] = my_w;
@@ -352,6 +358,57 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
             R.rinv[i] = __ldcg(a.rinv + i);
             R.sgw[i] = __ldcg(a.rsgw + i);
         }
+    } else if (T == 1 && !a.route_only) {
+        // One token (decode): the routing warp builds the tables from its
+        // registers -- one pair per picked expert held here, shared expert
+        // first, then the picks in top-k order.
+        if (warp == 0) {
+            int e;
+            float w, sg;
+            route_token<PER>(a, Ld, 0, R.idx, R.w, R.rinv, R.sgw, cta0, (st && lane == 0) ? st : nullptr, &e, &w,
+                             &sg);
+            const int hs = Ld.sh_gate ? 1 : 0;
+            const bool loc = lane < K && e >= a.lo && e < a.hi;
+            const unsigned locs = __ballot_sync(0xffffffffu, loc);
+            const int g = hs + __popc(locs & ((1u << lane) - 1u));
+            if (loc) {
+                R.ptok[g] = 0;
+                R.pw[g] = w;
+                R.gexp[g] = e;
+                R.goff[g] = g;
+                R.gcnt[g] = 1;
+                R.gcpre[g] = g;
+                R.chunk[g] = make_int4(e, g, 1, 0);
+                if (!Ld.gate_base) {
+                    R.ptr[3 * (e - a.lo) + 0] = expert_ptr(Ld.gate, nullptr, e, E);
+                    R.ptr[3 * (e - a.lo) + 1] = expert_ptr(Ld.up, nullptr, e, E);
+                    R.ptr[3 * (e - a.lo) + 2] = expert_ptr(Ld.down, nullptr, e, E);
+                }
+            }
+            if (lane == 0) {
+                if (hs) {
+                    R.ptok[0] = 0;
+                    R.pw[0] = sg;
+                    R.gexp[0] = E;
+                    R.goff[0] = 0;
+                    R.gcnt[0] = 1;
+                    R.gcpre[0] = 0;
+                    R.chunk[0] = make_int4(E, 0, 1, 0);
+                }
+                const int ng = hs + __popc(locs);
+                R.gcpre[ng] = ng;
+                R.scal[0] = ng;
+                R.scal[1] = ng;
+                R.scal[2] = ng;
+                if (cta0 && a.stats) {
+                    a.stats[2 * l] = ng;
+                    a.stats[2 * l + 1] = ng;
+                }
+            }
+            if (st && lane == 0) st[21] = globaltimer();
+        }
+        named_sync(BAR_CONS, ST_CONS);
+        return;
     } else {
         for (int t = warp; t < T; t += 8)
             route_token<PER>(a, Ld, t, R.idx, R.w, R.rinv, R.sgw, cta0, (st && tid == 0) ? st : nullptr);
@@ -780,11 +837,23 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 bulk_g2s(st + (size_t)TC * I * 2, a.as + (size_t)ci.p0 * (I / 32), (unsigned)(ci.np * (I / 8)),
                          da + d.slot);
             };
+            if (l + 1 < a.L) issue_router(l + 1);  // consumers are past phase A
+            pstamp(l, 13);
+            // The down weights are needed only after the next grid barrier:
+            // request them once this CTA's gate/up stages have landed, so they
+            // do not compete with them for HBM.
+            if (dpre > 0 && nch * R > bx) {
+                if (lane < C::SPI && lane < NS_G) {
+                    // stage issued `lane + 1` positions before the cursor: its slot
+                    // is that of NS_G - 1 - lane positions ahead, one lap earlier
+                    const Ring g = gR.ahead(NS_G - 1 - lane, NS_G);
+                    swait(gfull + g.slot, (unsigned)(g.phase ^ 1));
+                }
+                __syncwarp();
+            }
             if (lane < dpre) issue_dw(dR.ahead(lane, NS_D), lane);
             __syncwarp();
             pstamp(l, 12);
-            if (l + 1 < a.L) issue_router(l + 1);  // consumers are past phase A
-            pstamp(l, 13);
             // the intermediate of every CTA is complete after grid barrier (phase B)
             if (lane == 0) {
                 const int bidx = l * nbl + (dist ? 2 : 1);
