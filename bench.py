@@ -37,6 +37,7 @@ GATE_B = I * H // 256 * 144      # one expert's gate (= up) matrix, bytes
 DOWN_B = H * I // 256 * 210      # one expert's down matrix, bytes
 EXPERT_B = 2 * GATE_B + DOWN_B   # 2,039,808
 N_INPUTS = 16
+BATCH2 = 64                      # second batch size of config 5, reported beside the headline
 
 
 def peaks():
@@ -275,7 +276,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     T = args.batch
-    st = bb.ExpertStack(n_layers=args.layers, hidden=H, inter=I, n_experts=E, top_k=K_TOP, max_tokens=T,
+    T2 = BATCH2 if (T != BATCH2 and not args.quick) else None  # secondary batch size, same stack
+    st = bb.ExpertStack(n_layers=args.layers, hidden=H, inter=I, n_experts=E, top_k=K_TOP,
+                        max_tokens=max(T, T2 or 0),
                         shared_expert=True, norm_eps=1e-6, seed=args.seed, rank=rank, world=world)
     if world > 1:
         st.connect_peers(dist)
@@ -343,6 +346,32 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     ms_e2e = e2.elapsed_time(e3)
     clk = clocks.stop()
 
+    # the same stack at the second batch size (config 5 names batch 1 and 64)
+    batch2 = None
+    if T2:
+        inputs2 = [bb.synth_normal(T2 * H, 1.0, args.seed, 950 + i, device=dev).view(T2, H) for i in range(4)]
+        h2 = torch.empty(T2, H, dtype=torch.float32, device=dev)
+        for i in range(3):
+            h2.copy_(inputs2[i % 4])
+            st.step(h2)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n2 = max(3, args.steps // 5)
+        f0.record(stream)
+        for i in range(n2):
+            h2.copy_(inputs2[i % 4])
+            st.step(h2)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms2 = f0.elapsed_time(f1) / n2
+        g2, p2 = st.routing_stats()
+        b2 = sum(sum(layer_bytes(int(g), int(p), T2).values()) for g, p in zip(g2, p2))
+        batch2 = {"batch": T2, "steps": n2, "ms_per_step": ms2, "tok_s": T2 / (ms2 * 1e-3),
+                  "step_hbm_gbs": b2 / (ms2 * 1e-3) / 1e9, "experts_per_layer": float(np.mean(g2))}
+
     # phase durations (a profiled launch of the same step: every CTA records
     # %globaltimer at its phase points) and routing stats
     h.copy_(inputs[0])
@@ -352,15 +381,19 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     assert bb.device_error() == 0, "device-side wait timed out"
 
     if dist is not None:
-        t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=dev)
+        t = torch.tensor([ms, ms_e2e, batch2["ms_per_step"] if batch2 else 0.0], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, ms_e2e = float(t[0]), float(t[1])
+        if batch2:
+            batch2["ms_per_step"] = float(t[2])
+            batch2["tok_s"] = T2 / (batch2["ms_per_step"] * 1e-3)
     if rank != 0:
         st.close()
         dist.destroy_process_group()
         return 0
 
     hbm_peak, peak_kind = peaks()
+    launches = args.steps * st.launches_per_step(T)
     ms_step = ms / args.steps
     value = T / (ms_step * 1e-3)
     bytes_per_layer = [layer_bytes(int(g), int(p), T) for g, p in zip(groups, pairs)]
@@ -379,6 +412,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
         except Exception:
             traffic = None
     timeline = layer_timeline(stamps)
+
+    matvec = None
+    if world == 1:
+        st.close()  # free the stack before the GEMV weights
+        matvec = matvec_bench(dev, hbm_peak)
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -402,14 +440,50 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
         "cpu_baseline": cpu,
         "e2e": {"value": T / (ms_e2e / args.steps * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": T * H * 4,
                 "d2h_bytes_per_step": T * H * 4},
-        "gpu_launches": args.steps * st.launches_per_step(T),
+        "gpu_launches": launches,
         "clocks": clk,
+        "batch2": batch2,
+        "matvec": matvec,
     }
     print(json.dumps(line), flush=True)
     st.close()
     if dist is not None:
         dist.destroy_process_group()
     return 0
+
+
+def matvec_bench(dev, hbm_peak) -> dict:
+    """The expert matvec kernels on their largest benchmark shape (config 2's
+    248320 x 2048 output head, Q6_K and Q4_K): CUDA-event time of back-to-back
+    bread_matvec_f32 launches alternating between two weight copies (417 MB /
+    286 MB each, > L2), algorithmic bytes = weights + x + y."""
+    import torch
+
+    import breadv2_b200 as bb
+
+    out = {}
+    rows, cols = 248320, 2048
+    x = bb.synth_normal(cols, 1.0, 7, 8, device=dev)
+    y = torch.empty(rows, device=dev)
+    for name, qt, bb_ in (("q6k_head", 14, 210), ("q4k_head", 12, 144)):
+        nb = rows * cols // 256
+        ws = [bb.synth_blocks(nb, qt, 7, 10 + i, device=dev) for i in range(2)]
+        for i in range(3):
+            bb.matvec_f32(ws[i % 2], x, rows, cols, qt, y=y)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 10
+        e0.record()
+        for i in range(n):
+            bb.matvec_f32(ws[i % 2], x, rows, cols, qt, y=y)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / n * 1e3
+        gbs = (nb * bb_ + 4 * cols + 4 * rows) / (us * 1e-6) / 1e9
+        out[name] = {"shape": [rows, cols], "us": us, "GB_s": gbs, "frac": gbs / hbm_peak}
+        del ws
+    torch.cuda.empty_cache()
+    return out
 
 
 def main(argv=None) -> int:

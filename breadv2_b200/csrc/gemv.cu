@@ -73,7 +73,8 @@ __device__ __forceinline__ void quantise_to_smem(const void *x, int T, int cols,
         const float v = IN_HALF ? __half2float(reinterpret_cast<const __half *>(x)[idx])
                                 : reinterpret_cast<const float *>(x)[idx];
         const int q = quant32(v, xs + gi, lane);
-        xq[idx] = (int16_t)q;
+        const int t = idx / cols, e = idx - t * cols;
+        xq[(size_t)t * cols + xq_pos(e)] = (int16_t)q;
     }
 }
 

@@ -924,7 +924,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 const float ss = warp_sum(v * v);
                 if (lane == 0) a.ssq[gi] = ss;
                 const int q = quant32(v, a.xs + gi, lane);
-                a.xq[(size_t)gi * 32 + lane] = (int16_t)q;
+                const int e = gi * 32 + lane, t = e / H;  // H: a power of two
+                a.xq[(size_t)t * H + xq_pos(e - t * H)] = (int16_t)q;
             }
         }
         if (stamp) stamp_at(l, 16);
@@ -1206,7 +1207,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 for (int j = warp; j < ci.np; j += 8) {
                     const size_t p = (size_t)(ci.p0 + j);
                     const int q = quant32(abuf[j * MOE_ROWTILE + lane], a.as + p * (I / 32) + rt, lane);
-                    a.aq[p * I + (size_t)rt * MOE_ROWTILE + lane] = (int16_t)q;
+                    a.aq[p * I + xq_pos(rt * MOE_ROWTILE + lane)] = (int16_t)q;
                 }
                 named_sync(BAR_CONS, ST_CONS);
             }

@@ -101,6 +101,22 @@ __device__ __forceinline__ int quant32(float v, float *scale, int lane)
 // ---------------------------------------------------------------------------
 // lane dots
 // ---------------------------------------------------------------------------
+// Layout of quantised activations (per token, in global and shared memory):
+// the eight 16-byte pieces of every 128-byte chunk (64 values) are rotated by
+// the chunk index, so value e of the token sits at xq_pos(e).  The lanes of a
+// quarter-warp read eight different chunks, piece by piece: with the rotation
+// they hit eight different bank groups instead of one.  Positions are
+// relative to the token's first value (rows are a multiple of 64 values).
+__host__ __device__ __forceinline__ constexpr int xq_pos(int e)
+{
+    return (e & ~63) | ((((e >> 3) + (e >> 6)) & 7) << 3) | (e & 7);
+}
+// The 8 values e .. e+7 (e a multiple of 8) of a token stored as above.
+__device__ __forceinline__ int4 xq_piece(const int16_t *tok, int e)
+{
+    return *reinterpret_cast<const int4 *>(tok + xq_pos(e));
+}
+
 // One lane's activation slice for one token: 64 int16 (two per int).
 struct XSlice {
     int v[32];
@@ -110,15 +126,15 @@ struct XSlice {
 
 // Q4_K lane (block b, pair g): block elements 64g..64g+63, i.e. sub-blocks 2g
 // (low nibbles of qs[32g..32g+31]) and 2g+1 (high nibbles).
-// xq/xs: the token's int16 values and per-32 scales; e0 = 256*b + 64*g.
+// xq/xs: the token's int16 values (xq_pos layout) and per-32 scales;
+// e0 = 256*b + 64*g.
 // rs multiplies the group scales (the RMS-normalisation factor of the token).
 __device__ __forceinline__ void load_slice_q4k(XSlice &X, const int16_t *xq, const float *xs, int e0,
                                                float rs = 1.0f)
 {
-    const int4 *p = reinterpret_cast<const int4 *>(xq + e0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const int4 t = p[i];
+        const int4 t = xq_piece(xq, e0 + 8 * i);
         X.v[4 * i + 0] = t.x;
         X.v[4 * i + 1] = t.y;
         X.v[4 * i + 2] = t.z;
@@ -179,8 +195,7 @@ __device__ __forceinline__ void load_slice_q6k(XSlice &X, const int16_t *xq, con
 {
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-        const int4 *p = reinterpret_cast<const int4 *>(xq + base + 32 * r + 16 * g);
-        const int4 t0 = p[0], t1 = p[1];
+        const int4 t0 = xq_piece(xq, base + 32 * r + 16 * g), t1 = xq_piece(xq, base + 32 * r + 16 * g + 8);
         X.v[8 * r + 0] = t0.x;
         X.v[8 * r + 1] = t0.y;
         X.v[8 * r + 2] = t0.z;
