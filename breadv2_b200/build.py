@@ -25,8 +25,9 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC", "-Xcompiler", "-O2",
          "--expt-relaxed-constexpr", f"-I{INCLUDE}", "-Wno-deprecated-gpu-targets"]
 
-SOURCES = ["errors.cu", "gemv.cu", "glue.cu", "moe.cu", "noalloc.cu", "stack.cu", "synth.cu"]
-HEADERS = ["common.cuh", "ptx.cuh", "qdot.cuh", "moe.cuh"]
+SOURCES = ["errors.cu", "gemv.cu", "glue.cu", "moe.cu", "moe_h1.cu", "moe_h2.cu", "moe_h4.cu", "moe_h8.cu",
+           "moe_h16.cu", "noalloc.cu", "stack.cu", "synth.cu"]
+HEADERS = ["common.cuh", "ptx.cuh", "qdot.cuh", "moe.cuh", "moe_kernel.cuh"]
 
 
 def _stale(target: str, deps: list[str]) -> bool:
@@ -57,7 +58,7 @@ def build(verbose: bool = False, force: bool = False, ptxas_v: bool = False) -> 
         if force or ptxas_v or _stale(o, [s, *hdrs, __file__]):
             extra = ["-Xptxas", "-v"] if ptxas_v else []
             jobs.append([NVCC, *ARCH, *FLAGS, *extra, "-c", s, "-o", o])
-    with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
+    with cf.ThreadPoolExecutor(max_workers=min(12, os.cpu_count() or 4)) as ex:
         list(ex.map(lambda c: _run(c, verbose or ptxas_v), jobs))
     if force or jobs or _stale(LIB, objs):
         _run([NVCC, *ARCH, "-rdc=true", "-shared", "-Xcompiler", "-fPIC", *objs, "-o", LIB, "-lcudart"], verbose)

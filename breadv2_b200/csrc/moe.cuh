@@ -1,4 +1,4 @@
-// moe.cuh -- shared definitions of the persistent MoE step kernel (moe.cu)
+// moe.cuh -- shared definitions of the persistent MoE step kernel (moe_kernel.cuh)
 // and its callers (the MoE block entry points in moe.cu, the stack executor
 // in stack.cu, the no-alloc entry point in noalloc.cu).
 #pragma once
