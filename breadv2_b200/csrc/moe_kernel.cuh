@@ -118,8 +118,9 @@ __device__ __forceinline__ void grid_barrier(const StepArgs &a, int idx, int tid
 {
     named_sync(BAR_CONS, ST_CONS);
     if (tid == 0) {
-        __threadfence();
-        atomicAdd(a.ctrl + CTRL_GRID, 1ull);
+        // release at gpu scope, cumulative over the CTA's writes ordered by the
+        // barrier above; the poll acquires
+        red_release_gpu(a.ctrl + CTRL_GRID, 1ull);
         wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(idx + 1) * gridDim.x, false, GRID_WAIT_NS);
     }
     named_sync(BAR_CONS, ST_CONS);
@@ -907,14 +908,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         auto xin = [&](size_t i) -> float {
             float v = __ldcg(src + i);
             if (pmb)
-                for (int r = 0; r < a.ep_world; ++r) v += __ldcv(pmb + (size_t)r * TH + i);
+                for (int r = 0; r < a.ep_world; ++r) v += __ldcg(pmb + (size_t)r * TH + i);
             return v;
         };
         auto xin4 = [&](size_t i) -> float4 {  // i: a multiple of 4
             float4 v = __ldcg(reinterpret_cast<const float4 *>(src + i));
             if (pmb)
                 for (int r = 0; r < a.ep_world; ++r) {
-                    const float4 q = __ldcv(reinterpret_cast<const float4 *>(pmb + (size_t)r * TH + i));
+                    const float4 q = __ldcg(reinterpret_cast<const float4 *>(pmb + (size_t)r * TH + i));
                     v.x += q.x;
                     v.y += q.y;
                     v.z += q.z;
@@ -1320,13 +1321,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 }
                 if (stamp) stamp_at(l, 23);
                 if (ep) {
-                    // one system-scope release by thread 0, after the CTA barrier
-                    // that orders every thread's partial stores before it
+                    // system-scope releases by thread 0, after the CTA barrier
+                    // that orders every thread's partial stores before them
                     named_sync(BAR_CONS, ST_CONS);
-                    if (tid == 0) {
-                        __threadfence_system();
+                    if (tid == 0)
                         for (int p = 0; p < a.ep_world; ++p) red_release_sys(ep_counter(a, p, slot_l), 1ull);
-                    }
                 }
                 named_sync(BAR_CONS, ST_CONS);
             }
@@ -1349,7 +1348,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             for (int i = tid; i < T * MOE_RT3; i += ST_CONS) {
                 const size_t o = (size_t)(i / MOE_RT3) * H + (size_t)it3 * MOE_RT3 + i % MOE_RT3;
                 float v = __ldcg(src + o);
-                for (int r = 0; r < a.ep_world; ++r) v += __ldcv(pmb + (size_t)r * TH + o);
+                for (int r = 0; r < a.ep_world; ++r) v += __ldcg(pmb + (size_t)r * TH + o);
                 a.y[o] = v;
             }
     }

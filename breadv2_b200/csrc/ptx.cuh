@@ -113,6 +113,11 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
+// Release-add at gpu scope (the grid-barrier counter).
+__device__ __forceinline__ void red_release_gpu(unsigned long long *p, unsigned long long v)
+{
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 // Release-add at system scope (arrival counters in peers' memory over NVLink).
 __device__ __forceinline__ void red_release_sys(unsigned long long *p, unsigned long long v)
 {
