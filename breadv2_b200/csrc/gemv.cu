@@ -56,6 +56,7 @@ struct GemvSmem {
     {
         size_t b = align_up((size_t)T * Geo<QT, NB>::COLS * 2, 16);           // xq
         b += align_up((size_t)T * Geo<QT, NB>::COLS / 32 * 4, 16);             // xs
+        b += align_up((size_t)T * Geo<QT, NB>::COLS / 16 * 4, 16);             // xs16
         b += (size_t)GEMV_WARPS * GEMV_STAGES * chunk + 16;                    // stages + tail pad
         b = align_up(b, 8) + GEMV_WARPS * GEMV_STAGES * 8;                     // mbarriers
         return b;
@@ -64,8 +65,8 @@ struct GemvSmem {
 
 // Quantise T x cols activations (fp32 or fp16) into shared memory.
 template <bool IN_HALF>
-__device__ __forceinline__ void quantise_to_smem(const void *x, int T, int cols, int16_t *xq, float *xs, int warp,
-                                                 int nwarps, int lane)
+__device__ __forceinline__ void quantise_to_smem(const void *x, int T, int cols, int16_t *xq, float *xs, int *xs16,
+                                                 int warp, int nwarps, int lane)
 {
     const int groups = T * cols / 32;
     for (int gi = warp; gi < groups; gi += nwarps) {
@@ -75,6 +76,8 @@ __device__ __forceinline__ void quantise_to_smem(const void *x, int T, int cols,
         const int q = quant32(v, xs + gi, lane);
         const int t = idx / cols, e = idx - t * cols;
         xq[(size_t)t * cols + xq_pos(e)] = (int16_t)q;
+        const int s16 = sum16(q);
+        if ((lane & 15) == 0) xs16[2 * gi + (lane >> 4)] = s16;
     }
 }
 
@@ -87,13 +90,15 @@ gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__r
     constexpr size_t CHUNK = GemvSmem<QT, NB>::chunk;
     constexpr int GEMV_CH = GemvSmem<QT, NB>::CH;
     extern __shared__ __align__(128) uint8_t smem[];
+    const size_t o_xs = align_up((size_t)T * G::COLS * 2, 16);
+    const size_t o_xs16 = o_xs + align_up((size_t)T * G::COLS / 32 * 4, 16);
+    const size_t o_st = o_xs16 + align_up((size_t)T * G::COLS / 16 * 4, 16);
     int16_t *xq = reinterpret_cast<int16_t *>(smem);
-    float *xs = reinterpret_cast<float *>(smem + align_up((size_t)T * G::COLS * 2, 16));
-    uint8_t *stages = smem + align_up((size_t)T * G::COLS * 2, 16) + align_up((size_t)T * G::COLS / 32 * 4, 16);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(
-        smem + align_up(align_up((size_t)T * G::COLS * 2, 16) + align_up((size_t)T * G::COLS / 32 * 4, 16) +
-                            (size_t)GEMV_WARPS * GEMV_STAGES * CHUNK + 16,
-                        8));
+    float *xs = reinterpret_cast<float *>(smem + o_xs);
+    int *xs16 = reinterpret_cast<int *>(smem + o_xs16);
+    uint8_t *stages = smem + o_st;
+    uint64_t *bars =
+        reinterpret_cast<uint64_t *>(smem + align_up(o_st + (size_t)GEMV_WARPS * GEMV_STAGES * CHUNK + 16, 8));
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint8_t *my_stage = stages + (size_t)warp * GEMV_STAGES * CHUNK;
@@ -122,7 +127,7 @@ gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__r
     if (lane == 0)
         for (int c = 0; c < min(GEMV_STAGES, nchunks); ++c) issue(c);
 
-    quantise_to_smem<IN_HALF>(x, T, G::COLS, xq, xs, warp, GEMV_WARPS, lane);
+    quantise_to_smem<IN_HALF>(x, T, G::COLS, xq, xs, xs16, warp, GEMV_WARPS, lane);
     __syncthreads();
 
     // lane geometry
@@ -166,16 +171,26 @@ gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__r
                 if (ONE_TOKEN) {
                     acc[0] += QT == BREAD_QTYPE_Q4_K ? q4k_lane_dot(blk, sub, X1[cp])
                                                      : q6k_lane_dot(blk, sub >> 1, sub & 1, L6, X1[cp]);
-                } else {
+                } else if (QT == BREAD_QTYPE_Q4_K) {
+                    // several tokens: decode the lane's weights once, then one
+                    // dot per token from its slice in shared memory
+                    Q4W W;
+                    q4k_lane_w(W, blk, sub);
+                    const int e0 = QK * (cp * 8 + bb) + 64 * sub;
 #pragma unroll
-                    for (int t = 0; t < GEMV_TMAX; ++t) {
-                        if (t < T) {
-                            XSlice X;
-                            slice_of(X, t, cp);
-                            acc[t] += QT == BREAD_QTYPE_Q4_K ? q4k_lane_dot(blk, sub, X)
-                                                             : q6k_lane_dot(blk, sub >> 1, sub & 1, L6, X);
-                        }
-                    }
+                    for (int t = 0; t < GEMV_TMAX; ++t)
+                        if (t < T)
+                            acc[t] += q4k_dot_w(W, xq + (size_t)t * G::COLS, xs + (size_t)t * G::COLS / 32,
+                                                xs16 + (size_t)t * G::COLS / 16, e0, 1.0f);
+                } else {
+                    Q6W W;
+                    q6k_lane_w(W, blk, sub >> 1, sub & 1, L6);
+                    const int base = QK * (cp * 8 + bb) + 128 * (sub >> 1);
+#pragma unroll
+                    for (int t = 0; t < GEMV_TMAX; ++t)
+                        if (t < T)
+                            acc[t] += q6k_dot_w(W, xq + (size_t)t * G::COLS, xs + (size_t)t * G::COLS / 32,
+                                                xs16 + (size_t)t * G::COLS / 16, base, sub & 1, 1.0f);
                 }
             }
 #pragma unroll

@@ -293,4 +293,130 @@ __device__ __forceinline__ float q6k_lane_dot(const uint8_t *blk, int h, int g, 
     return d * acc;
 }
 
+// ---------------------------------------------------------------------------
+// weights-stationary lane dots: a lane decodes its share of a block row once
+// and applies it to several tokens.  The activation side is the same int16
+// slice (xq_pos layout) with its group scales xs (per 32 values) and exact
+// int sums xs16 (per 16 values) computed when the activations were quantised.
+// ---------------------------------------------------------------------------
+// Q4_K lane (block b, pair g): the 32 quant bytes of sub-blocks 2g, 2g+1 and
+// their factors d*sc (the high-nibble one carrying 1/16) and dmin*m.
+struct Q4W {
+    uint32_t w[8];
+    float a0, a1, b0, b1;
+};
+__device__ __forceinline__ void q4k_lane_w(Q4W &W, const uint8_t *blk, int g)
+{
+    const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
+    const uint4 qa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * g);
+    const uint4 qb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * g);
+    W.w[0] = qa.x;
+    W.w[1] = qa.y;
+    W.w[2] = qa.z;
+    W.w[3] = qa.w;
+    W.w[4] = qb.x;
+    W.w[5] = qb.y;
+    W.w[6] = qb.z;
+    W.w[7] = qb.w;
+    const uint32_t sh = 16u * (uint32_t)(g & 1);
+    const uint32_t A = hd.y >> sh, B = hd.z >> sh, C = hd.w >> sh;
+    uint32_t scp, mp;
+    if (g >= 2) {
+        scp = (C & 0x0F0Fu) | ((A >> 2) & 0x3030u);
+        mp = ((C >> 4) & 0x0F0Fu) | ((B >> 2) & 0x3030u);
+    } else {
+        scp = A & 0x3F3Fu;
+        mp = B & 0x3F3Fu;
+    }
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&hd.x));
+    W.a0 = dd.x * u2f_small(scp & 0xFFu);
+    W.a1 = dd.x * (u2f_small((scp >> 8) & 0xFFu) * 0.0625f);
+    W.b0 = dd.y * u2f_small(mp & 0xFFu);
+    W.b1 = dd.y * u2f_small((mp >> 8) & 0xFFu);
+}
+// One token's dot with a decoded Q4_K lane; e0 = 256*b + 64*g, rs scales xs.
+__device__ __forceinline__ float q4k_dot_w(const Q4W &W, const int16_t *xq, const float *xs, const int *xs16, int e0,
+                                           float rs)
+{
+    int p0 = 0, p1 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int4 t = xq_piece(xq, e0 + 8 * k);
+        const uint32_t l0 = W.w[2 * k] & 0x0F0F0F0Fu, l1 = W.w[2 * k + 1] & 0x0F0F0F0Fu;
+        p0 = dp2a_lo(t.x, l0, p0);
+        p0 = dp2a_hi(t.y, l0, p0);
+        p0 = dp2a_lo(t.z, l1, p0);
+        p0 = dp2a_hi(t.w, l1, p0);
+        const int4 u = xq_piece(xq, e0 + 32 + 8 * k);
+        const uint32_t h0 = W.w[2 * k] & 0xF0F0F0F0u, h1 = W.w[2 * k + 1] & 0xF0F0F0F0u;
+        p1 = dp2a_lo(u.x, h0, p1);
+        p1 = dp2a_hi(u.y, h0, p1);
+        p1 = dp2a_lo(u.z, h1, p1);
+        p1 = dp2a_hi(u.w, h1, p1);
+    }
+    const int gi = e0 >> 5;
+    const float f0 = xs[gi] * rs, f1 = xs[gi + 1] * rs;
+    const int s0 = xs16[2 * gi] + xs16[2 * gi + 1], s1 = xs16[2 * gi + 2] + xs16[2 * gi + 3];
+    const float mins = fmaf(W.b1 * f1, (float)s1, (W.b0 * f0) * (float)s0);
+    return fmaf(W.a0 * f0, (float)p0, fmaf(W.a1 * f1, (float)p1, -mins));
+}
+
+// Q6_K lane (half h, l-group g): the 6-bit codes of its four runs and d*sc.
+struct Q6W {
+    uint32_t v[16];  // v[4r + i]: codes of run r, l = 16g + 4i .. 4i + 3
+    float s[4];
+};
+__device__ __forceinline__ void q6k_lane_w(Q6W &W, const uint8_t *blk, int h, int g, const Q6Lane &L)
+{
+    uint32_t A[4], B[4], Q[4];
+    ld16_shift(blk + 64 * h + 16 * g, L.sh, L.sel, A);
+    ld16_shift(blk + 64 * h + 32 + 16 * g, L.sh, L.sel, B);
+    ld16_shift(blk + 128 + 32 * h + 16 * g, L.sh, L.sel, Q);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        W.v[i] = (A[i] & 0x0F0F0F0Fu) | ((Q[i] << 4) & 0x30303030u);
+        W.v[4 + i] = (B[i] & 0x0F0F0F0Fu) | ((Q[i] << 2) & 0x30303030u);
+        W.v[8 + i] = ((A[i] >> 4) & 0x0F0F0F0Fu) | (Q[i] & 0x30303030u);
+        W.v[12 + i] = ((B[i] >> 4) & 0x0F0F0F0Fu) | ((Q[i] >> 2) & 0x30303030u);
+    }
+    const uint32_t *sq = reinterpret_cast<const uint32_t *>(blk + 192 + 8 * h - L.sh);
+    const uint32_t w0 = sq[0], w1 = sq[1], w2 = sq[2];
+    const uint32_t slo = prmt(w0, w1, L.sel), shi = prmt(w1, w2, L.sel);
+    const float d = __half2float(*reinterpret_cast<const __half *>(blk + 208));
+    W.s[0] = d * s2f_small((int)prmt(slo, 0u, L.ssel[0]));
+    W.s[1] = d * s2f_small((int)prmt(slo, 0u, L.ssel[1]));
+    W.s[2] = d * s2f_small((int)prmt(shi, 0u, L.ssel[0]));
+    W.s[3] = d * s2f_small((int)prmt(shi, 0u, L.ssel[1]));
+}
+// One token's dot with a decoded Q6_K lane; base = 256*b + 128*h.
+__device__ __forceinline__ float q6k_dot_w(const Q6W &W, const int16_t *xq, const float *xs, const int *xs16, int base,
+                                           int g, float rs)
+{
+    float acc = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int e = base + 32 * r + 16 * g;
+        const int4 t0 = xq_piece(xq, e), t1 = xq_piece(xq, e + 8);
+        int p = dp2a_lo(t0.x, W.v[4 * r], 0);
+        p = dp2a_hi(t0.y, W.v[4 * r], p);
+        p = dp2a_lo(t0.z, W.v[4 * r + 1], p);
+        p = dp2a_hi(t0.w, W.v[4 * r + 1], p);
+        p = dp2a_lo(t1.x, W.v[4 * r + 2], p);
+        p = dp2a_hi(t1.y, W.v[4 * r + 2], p);
+        p = dp2a_lo(t1.z, W.v[4 * r + 3], p);
+        p = dp2a_hi(t1.w, W.v[4 * r + 3], p);
+        acc = fmaf(W.s[r] * (xs[e >> 5] * rs), (float)(p - 32 * xs16[e >> 4]), acc);
+    }
+    return acc;
+}
+
+// Exact int sums of a quantised group's two 16-value halves (full warp, one
+// value per lane): lanes 0 and 16 return their half's sum.
+__device__ __forceinline__ int sum16(int q)
+{
+#pragma unroll
+    for (int o = 8; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    return q;
+}
+
 }  // namespace bread
