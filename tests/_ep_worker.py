@@ -18,9 +18,9 @@ def main():
     import datetime
 
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
-    cfg = dict(n_layers=int(os.environ.get("EP_LAYERS", "3")), hidden=1024, inter=512, n_experts=32, top_k=4,
-               max_tokens=8, shared_expert=True, norm_eps=1e-6, seed=21)
     T = int(os.environ.get("EP_T", "4"))
+    cfg = dict(n_layers=int(os.environ.get("EP_LAYERS", "3")), hidden=1024, inter=512, n_experts=32, top_k=4,
+               max_tokens=max(8, T), shared_expert=True, norm_eps=1e-6, seed=21)
     st = bb.ExpertStack(**cfg, rank=rank, world=world)
     st.connect_peers(dist)
     h0 = bb.synth_normal(T * 1024, 1.0, 21, 7, device="cuda").view(T, 1024)

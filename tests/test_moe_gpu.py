@@ -20,7 +20,7 @@ MARGIN = 1e-4  # logit gap below which fp32 summation order may legally reorder
 class Layer:
     """Synthetic MoE layer on the device (bread_synth_*), pointer tables included."""
 
-    def __init__(self, cuda, H, I, E, shared=True, sg_vec=True, seed=5, stack_layer=0):
+    def __init__(self, cuda, H, I, E, shared=True, sg_vec=True, seed=5, stack_layer=0, router_std=0.02):
         self.H, self.I, self.E = H, I, E
         sid = lambda kind, e: (stack_layer << 32) | (kind << 24) | e  # noqa: E731
         nb_g, nb_d = I * H // 256, H * I // 256
@@ -32,7 +32,7 @@ class Layer:
             self.shared = (bb.synth_blocks(nb_g, 12, seed, sid(3, 0), device=cuda),
                            bb.synth_blocks(nb_g, 12, seed, sid(4, 0), device=cuda),
                            bb.synth_blocks(nb_d, 14, seed, sid(5, 0), device=cuda))
-        self.W_r = bb.synth_normal(E * H, 0.02, seed, sid(6, 0), device=cuda).view(E, H)
+        self.W_r = bb.synth_normal(E * H, router_std, seed, sid(6, 0), device=cuda).view(E, H)
         self.w_sg = bb.synth_normal(H, 0.02, seed, sid(7, 0), half=True, device=cuda) if sg_vec else None
         self.tabs = [bb.pointer_table(t, cuda) for t in (self.gate, self.up, self.down)]
 
@@ -54,7 +54,10 @@ class Layer:
         return out, r
 
 
-def check_routing(orc, x, W_r, w_sg, top_k, idx, w, sg):
+def check_routing(orc, x, W_r, w_sg, top_k, idx, w, sg, w_rtol=1e-5):
+    """w_rtol: a softmax weight's relative error is its logit's absolute error,
+    and fp32 summation noise in a logit grows with the logit's magnitude, so
+    routers with larger weights get a proportionally larger tolerance."""
     xi = x.cpu().numpy()
     ridx, rw, rsg, _ = orc.route(xi, W_r.cpu().numpy(), None if w_sg is None else w_sg.cpu().numpy().view(np.uint16),
                                  top_k)
@@ -63,7 +66,7 @@ def check_routing(orc, x, W_r, w_sg, top_k, idx, w, sg):
     assert ok.mean() > 0.9, "seeded inputs should be mostly well separated"
     gi, gw = idx.cpu().numpy(), w.cpu().numpy()
     assert np.array_equal(gi[ok], ridx[ok])
-    np.testing.assert_allclose(gw[ok], rw[ok], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(gw[ok], rw[ok], rtol=w_rtol, atol=1e-7)
     np.testing.assert_allclose(sg.cpu().numpy(), rsg, rtol=1e-5)
     return ridx, rw, rsg
 
@@ -128,9 +131,12 @@ def test_moe_ffn_golden(cuda, orc, golden):
     assert orc.rel_l2(out.cpu().numpy(), g["out"]) < TOL
 
 
-@pytest.mark.parametrize("T", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("T", [1, 2, 4, 8, 16, 32, 64])
 def test_moe_ffn_config(cuda, orc, T):
-    """Config 3 (T=1) and config 4's sweep: H=2048, 256 experts, top-8 + shared."""
+    """Config 3 (T=1) and config 4's sweep: H=2048, 256 experts, top-8 + shared.
+    T <= 8 routes from router rows held in shared memory; T > 8 tiles the
+    router over the grid and shares one ring arena between gate/up and down;
+    T > 16 also spreads the top-k selection over the grid."""
     H, I, E, K = 2048, 512, 256, 8
     L = getattr(test_moe_ffn_config, "_layer", None)
     if L is None:
@@ -141,6 +147,26 @@ def test_moe_ffn_config(cuda, orc, T):
     gi, gw, gs = idx.cpu().numpy(), w.cpu().numpy(), sg.cpu().numpy()
     es = L.host_set(orc, gi.ravel())
     ref = orc.moe_f64(es, x.cpu().numpy(), gi, gw, gs, H, I)
+    assert orc.rel_l2(out.cpu().numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("T", [1, 5, 24])
+def test_moe_ffn_wide_router(cuda, orc, T):
+    """512 experts, top-16 (the kernel's largest router): per-lane key arrays
+    twice as long as at 256 experts, on every routing path (one token, a few
+    tokens, grid-distributed selection)."""
+    H, I, E, K = 1024, 256, 512, 16
+    L = getattr(test_moe_ffn_wide_router, "_layer", None)
+    if L is None:
+        L = test_moe_ffn_wide_router._layer = Layer(cuda, H, I, E, seed=31, router_std=0.1)
+    x = bb.synth_normal(T * H, 1.0, 31, 100 + T, device=cuda).view(T, H)
+    out, (idx, w, sg) = L.ffn(x, K)
+    # router std 0.1 (logits ~3, five times the 0.02 router's): weights to 5e-5
+    check_routing(orc, x, L.W_r, L.w_sg, K, idx, w, sg, w_rtol=5e-5)
+    gi = idx.cpu().numpy()
+    assert all(len(set(r)) == K for r in gi.tolist())
+    es = L.host_set(orc, gi.ravel())
+    ref = orc.moe_f64(es, x.cpu().numpy(), gi, w.cpu().numpy(), sg.cpu().numpy(), H, I)
     assert orc.rel_l2(out.cpu().numpy(), ref) < TOL
 
 

@@ -54,12 +54,15 @@ def oracle_chain(orc, cfg, h0, n_layers):
     return h
 
 
-@pytest.mark.parametrize("T", [1, 3])
-def test_stack_small_vs_oracle(cuda, orc, T):
-    cfg = dict(hidden=512, inter=256, n_experts=16, top_k=4, seed=11, eps=1e-6)
-    st = bb.ExpertStack(n_layers=3, hidden=512, inter=256, n_experts=16, top_k=4, max_tokens=4, shared_expert=True,
-                        norm_eps=1e-6, seed=11)
-    h0 = bb.synth_normal(T * 512, 1.0, 11, 1000 + T, device=cuda).view(T, 512)
+@pytest.mark.parametrize("T,seed", [(1, 11), (3, 11), (12, 18), (24, 18)])
+def test_stack_small_vs_oracle(cuda, orc, T, seed):
+    """3 layers chained through the residual; T > 8 takes the tiled router and
+    the shared ring arena, T > 16 the grid-distributed top-k (seeds picked so
+    every token's routing is separated by more than fp32 noise)."""
+    cfg = dict(hidden=512, inter=256, n_experts=16, top_k=4, seed=seed, eps=1e-6)
+    st = bb.ExpertStack(n_layers=3, hidden=512, inter=256, n_experts=16, top_k=4, max_tokens=max(4, T),
+                        shared_expert=True, norm_eps=1e-6, seed=seed)
+    h0 = bb.synth_normal(T * 512, 1.0, seed, 1000 + T, device=cuda).view(T, 512)
     h = h0.clone()
     st.step(h)
     torch.cuda.synchronize()
@@ -79,6 +82,20 @@ def test_stack_config_size_two_layers(cuda, orc):
     torch.cuda.synchronize()
     ref = oracle_chain(orc, cfg, h0.cpu().numpy(), 2)
     assert orc.rel_l2(h.cpu().numpy(), ref) < TOL
+    st.close()
+
+
+def test_stack_config_size_batch64(cuda, orc):
+    """The bench's batched workload: full layer shapes, T=64, 2 layers."""
+    cfg = dict(hidden=2048, inter=512, n_experts=256, top_k=8, seed=3, eps=1e-6)
+    st = bb.ExpertStack(n_layers=2, max_tokens=64, seed=3)
+    h0 = bb.synth_normal(64 * 2048, 1.0, 3, 43, device=cuda).view(64, 2048)
+    h = h0.clone()
+    st.step(h)
+    torch.cuda.synchronize()
+    ref = oracle_chain(orc, cfg, h0.cpu().numpy(), 2)
+    assert orc.rel_l2(h.cpu().numpy(), ref) < TOL
+    assert bb.device_error() == 0
     st.close()
 
 

@@ -44,7 +44,7 @@ def _noalloc(tabs, W_r, w_sg, shared, x, out, I, K, idx, w, sg):
                                           p(sg), bb._s(None))
 
 
-@pytest.mark.parametrize("T", [1, 8])
+@pytest.mark.parametrize("T", [1, 8, 16])
 def test_noalloc_matches_workspace_entry(cuda, T):
     H, I, E, K = 2048, 512, 256, 8
     tabs, W_r, w_sg, shared, _keep = _layer(cuda, H, I, E, seed=17)
