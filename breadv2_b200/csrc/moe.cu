@@ -58,6 +58,17 @@ void step_bind_workspace(StepArgs &a, void *ws, const StepWs &L)
     a.rsgw = reinterpret_cast<float *>(b + L.rsgw);
     a.buf[0] = L.buf0 ? reinterpret_cast<float *>(b + L.buf0) : nullptr;
     a.buf[1] = L.buf1 ? reinterpret_cast<float *>(b + L.buf1) : nullptr;
+    auto ll = [&](size_t off) { return L.ll_end ? reinterpret_cast<unsigned long long *>(b + off) : nullptr; };
+    a.ll_pres = ll(L.ll_pres);
+    a.ll_lg = ll(L.ll_lg);
+    a.ll_a = ll(L.ll_a);
+    a.ll_as = ll(L.ll_as);
+    a.ll_h = L.ll_h ? ll(L.ll_h) : nullptr;
+    a.ll_pres_n = LL_GMAX;
+    a.ll_lg_n = (size_t)L.ll_T * (a.E + 1);
+    a.ll_a_n = (size_t)L.ll_T * (a.top_k + 1) * (a.I / 2);
+    a.ll_as_n = (size_t)L.ll_T * (a.top_k + 1) * (a.I / 32);
+    a.ll_h_n = (size_t)L.ll_T * a.H;
 }
 
 static bool nb_ok_h(int nb) { return nb == 1 || nb == 2 || nb == 4 || nb == 8 || nb == 16; }
@@ -115,6 +126,7 @@ static int moe_prepare(StepArgs &a, const float *x, const float *W_r, const void
     a.ep_world = 1;
     a.ep_tmax = T;
     step_bind_workspace(a, workspace, L);
+    a.ll_reset = L.ll_end;
     return BREAD_OK;
 }
 
@@ -159,6 +171,8 @@ extern "C" int bread_moe_ffn(const void *const *gate_ptrs, const void *const *up
     a.idx_out = idx_out;
     a.w_out = w_out;
     a.sg_out = sg_out;
-    BREAD_CUDA(cudaMemsetAsync(a.ctrl, 0, CTRL_BYTES, stream), "moe_ffn: reset control words");
+    // control words (and the flagged-exchange words, whose tags restart at 1)
+    BREAD_CUDA(cudaMemsetAsync(a.ctrl, 0, a.ll_reset > CTRL_BYTES ? a.ll_reset : CTRL_BYTES, stream),
+               "moe_ffn: reset control words");
     return step_launch(a, stream);
 }

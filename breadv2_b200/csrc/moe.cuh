@@ -49,10 +49,24 @@ struct StepLayer {
 };
 
 // Control words at the head of the workspace (u64 each): the grid-barrier
-// counter, the exit ticket and the launch epoch.  Zero before the first
-// launch; the last CTA of every launch resets the first two and advances the
-// epoch.
-enum { CTRL_GRID = 0, CTRL_EXIT = 1, CTRL_EPOCH = 2 };
+// counter, the exit ticket, the launch epoch and the layer sequence (tags of
+// the flagged exchange words, below).  Zero before the first launch; the last
+// CTA of every launch resets the first two, advances the epoch by one and the
+// layer sequence by the launch's layers.
+enum { CTRL_GRID = 0, CTRL_EXIT = 1, CTRL_EPOCH = 2, CTRL_SEQ = 3 };
+
+// Flagged exchange (decode launches of a few tokens on one GPU): the values
+// CTAs hand to one another inside a launch -- router logits, the quantised
+// gate/up intermediate, the residual stream between layers -- travel as 8-byte
+// words {payload (low 32 bits), tag (high 32 bits)}, stored and loaded as
+// single 64-bit accesses at gpu scope.  The tag of layer l of a launch is
+// layer sequence + l + 1, so a reader that polls a word until its tag matches
+// has waited for exactly that value: no grid barrier, and the wait and the
+// read are one load.  Buffers alternate by layer parity; every CTA also posts
+// one presence word per layer, awaited by all, which keeps any CTA from
+// running two layers ahead of another (the double buffering is then enough).
+constexpr int LL_TMAX = 8;    // tokens per launch of the flagged-exchange decode mode
+constexpr int LL_GMAX = 256;  // CTAs of such a launch (presence words)
 
 // Phase points recorded per layer and CTA by a profiled launch
 // (StepArgs::stamps, %globaltimer ns).  Consumer thread 0: 0 layer start,
@@ -69,9 +83,15 @@ constexpr int STAMPS = 24;
 constexpr size_t CTRL_BYTES = 256;
 
 // Global scratch of one step launch (byte offsets, each 256-byte aligned).
+// The flagged-exchange words (LL_TMAX tokens at most) follow the control
+// words.  A stack workspace (inter_layer_buffers) holds them beside the other
+// pieces, two parities; a one-block workspace holds one parity in the same
+// bytes as the barrier-mode pieces (a launch uses one mode) and the caller
+// zeroes [0, ll_end) before every launch.
 struct StepWs {
     size_t ctrl, logits, score, ssq, xq, xs, aq, as, ridx, rw, rinv, rsgw, buf0, buf1, total;
-    int PM;
+    size_t ll_pres, ll_lg, ll_a, ll_as, ll_h, ll_end;  // ll_end == 0: no flagged-exchange words
+    int PM, ll_T, ll_par;
     __host__ static StepWs make(int T, int H, int I, int E, int K, bool inter_layer_buffers)
     {
         StepWs w;
@@ -83,6 +103,19 @@ struct StepWs {
         };
         w.PM = T * (K + 1);
         w.ctrl = take(CTRL_BYTES);
+        w.ll_T = T < LL_TMAX ? T : LL_TMAX;
+        w.ll_par = inter_layer_buffers ? 2 : 1;
+        w.ll_pres = w.ll_lg = w.ll_a = w.ll_as = w.ll_h = w.ll_end = 0;
+        if (I > 0 && (inter_layer_buffers || T <= LL_TMAX)) {
+            const size_t pm = (size_t)w.ll_T * (K + 1), par = (size_t)w.ll_par;
+            w.ll_pres = take(par * LL_GMAX * 8);
+            w.ll_lg = take(par * w.ll_T * (E + 1) * 8);
+            w.ll_a = take(par * pm * (I / 2) * 8);
+            w.ll_as = take(par * pm * (I / 32) * 8);
+            w.ll_h = inter_layer_buffers ? take(par * w.ll_T * H * 8) : 0;
+            w.ll_end = o;
+            if (!inter_layer_buffers) o = w.ctrl + CTRL_BYTES;  // the barrier-mode pieces share these bytes
+        }
         w.logits = take((size_t)T * E * 4);
         w.score = take((size_t)T * 4);
         w.ssq = take((size_t)T * (H / 32) * 4);
@@ -96,7 +129,7 @@ struct StepWs {
         w.rsgw = take((size_t)T * 4);
         w.buf0 = inter_layer_buffers ? take((size_t)T * H * 4) : 0;
         w.buf1 = inter_layer_buffers ? take((size_t)T * H * 4) : 0;
-        w.total = o;
+        w.total = o > w.ll_end ? o : w.ll_end;
         return w;
     }
 };
@@ -104,6 +137,7 @@ struct StepWs {
 // Shared-memory layout of one launch (byte offsets), computed on the host.
 struct StepSmem {
     uint32_t rbuf, part, xsl, gring, abuf, dring, acc, bars, total;
+    uint32_t xloc, xf, ssql;  // flagged-exchange mode: quantised tokens, layer input / intermediate, group sums
     uint32_t r_idx, r_w, r_rinv, r_sgw, r_cnt, r_run, r_off, r_gexp, r_goff, r_gcnt, r_gcpre, r_ptok, r_pw, r_scal, r_ptr, r_chunk;
     uint32_t xslot, dslot;
     int NS_G, NS_D, RR, WPR;
@@ -150,6 +184,10 @@ struct StepArgs {
     float *as;
     int *ridx;                  // routing of the grid (large T): [T x k] experts and weights,
     float *rw, *rinv, *rsgw;    // [T] RMS factors and shared-gate weights
+    // flagged-exchange words [parity][...] (NULL: the workspace has none)
+    unsigned long long *ll_pres, *ll_lg, *ll_a, *ll_as, *ll_h;
+    size_t ll_pres_n, ll_lg_n, ll_a_n, ll_as_n, ll_h_n;  // words per parity
+    size_t ll_reset;            // host only: bytes from ctrl zeroed before a one-block launch
     // optional outputs (written by CTA 0)
     int *idx_out;
     float *w_out, *sg_out;

@@ -113,6 +113,35 @@ __device__ __forceinline__ void swait(uint64_t *bar, unsigned parity)
     flag_error(DEVERR_TIMEOUT);
 }
 
+// Flagged word *p once its tag equals `tag`: bounded poll (the grid-barrier
+// limit), giving up at once when a wait elsewhere on the device has failed.
+// Returns the payload (0 after a timeout, with the device error set).
+static __device__ __noinline__ uint32_t flagged_wait(const unsigned long long *p, uint32_t tag)
+{
+    unsigned long long t0 = 0;
+    for (unsigned i = 0;; ++i) {
+        const unsigned long long v = ld_flagged(p);
+        if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
+        if ((i & 31) == 31) {
+            if (dev_failed()) return 0u;
+            const unsigned long long now = globaltimer();
+            if (!t0) {
+                t0 = now;
+            } else if (now - t0 > GRID_WAIT_NS) {
+                flag_error(DEVERR_TIMEOUT);
+                return 0u;
+            }
+        }
+        if (i > 8) __nanosleep(32);
+    }
+}
+// Payload of an already loaded word, polling again only when its tag is not
+// the expected one (so a batch of loads is in flight together first).
+__device__ __forceinline__ uint32_t flagged_take(unsigned long long v, const unsigned long long *p, uint32_t tag)
+{
+    return (uint32_t)(v >> 32) == tag ? (uint32_t)v : flagged_wait(p, tag);
+}
+
 // Grid-wide barrier number `idx` of this launch (all 256 consumer threads).
 __device__ __forceinline__ void grid_barrier(const StepArgs &a, int idx, int tid)
 {
@@ -257,22 +286,44 @@ __device__ __forceinline__ ChunkInfo chunk_search(const RouteTabs &R, int c)
 // of the scaled logits (see below), renormalised weights, the shared gate's
 // sigmoid (0.5 without a gate vector, one_layer.cu:944,1889).  Writes
 // idx/w [t*K + k], rinv/sgw [t]; `outputs` also writes the caller's copies.
-template <int PER>
+// LLM (flagged-exchange mode): the logits (row E = the shared-gate score) are
+// flagged words at llg [t * (E + 1) + row] with tag `tag`, and the group sums
+// of squares sit in shared memory (ssq_l), computed by this CTA.
+template <int PER, bool LLM = false>
 __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *idx, float *w, float *rinv,
                             float *sgw, bool outputs, unsigned long long *st, int *pick_i = nullptr,
-                            float *pick_w = nullptr, float *pick_sg = nullptr)
+                            float *pick_w = nullptr, float *pick_sg = nullptr,
+                            const unsigned long long *llg = nullptr, const float *ssq_l = nullptr, uint32_t tag = 0)
 {
     const int lane = threadIdx.x & 31;
     const int H = a.H, E = a.E, K = a.top_k, HG = H / 32;
     float p[PER];
+    float ss = 0.0f, score = 0.0f;
+    if constexpr (LLM) {
+        const unsigned long long *row = llg + (size_t)t * (E + 1);
+        unsigned long long raw[PER];
 #pragma unroll
-    for (int j = 0; j < PER; ++j) {
-        const int e = lane + 32 * j;
-        p[j] = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
+        for (int j = 0; j < PER; ++j) {
+            const int e = lane + 32 * j;
+            raw[j] = e < E ? ld_flagged(row + e) : 0ull;
+        }
+        const unsigned long long rsc = Ld.w_sg ? ld_flagged(row + E) : 0ull;
+        for (int g = lane; g < HG; g += 32) ss += ssq_l[t * HG + g];
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int e = lane + 32 * j;
+            p[j] = e < E ? __uint_as_float(flagged_take(raw[j], row + e, tag)) : -INFINITY;
+        }
+        if (Ld.w_sg) score = __uint_as_float(flagged_take(rsc, row + E, tag));
+    } else {
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int e = lane + 32 * j;
+            p[j] = e < E ? __ldcg(a.logits + (size_t)t * E + e) : -INFINITY;
+        }
+        for (int g = lane; g < HG; g += 32) ss += __ldcg(a.ssq + t * HG + g);
+        score = Ld.w_sg ? __ldcg(a.score + t) : 0.0f;
     }
-    float ss = 0.0f;
-    for (int g = lane; g < HG; g += 32) ss += __ldcg(a.ssq + t * HG + g);
-    const float score = Ld.w_sg ? __ldcg(a.score + t) : 0.0f;
     ss = warp_sum(ss);
     const float r = a.norm_eps >= 0.0f ? rsqrtf(ss / (float)H + a.norm_eps) : 1.0f;
     if (st) st[19] = globaltimer();
@@ -342,13 +393,29 @@ __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *
 // barrier) and the CTA copies them.  Then the (token, expert) pairs are
 // grouped by expert: group 0 is the shared expert (all T tokens), then the
 // routed experts held here, pairs token-major inside each group.
-template <int PER, bool BIG>
+// LLM: the logits come as flagged words (llg, tag) and, before anything else,
+// warp 0 waits for the presence word of every CTA for this layer (pres).
+template <int PER, bool BIG, bool LLM = false>
 __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const RouteTabs &R, int l, bool cta0,
-                             unsigned long long *st, bool dist)
+                             unsigned long long *st, bool dist, const unsigned long long *llg = nullptr,
+                             const unsigned long long *pres = nullptr, const float *ssq_l = nullptr,
+                             uint32_t tag = 0)
 {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = a.T, E = a.E, K = a.top_k;
     const int EL = a.hi - a.lo;
+    if constexpr (LLM) {
+        if (warp == 0) {
+            const int G = gridDim.x;
+            unsigned long long raw[LL_GMAX / 32];
+#pragma unroll
+            for (int k = 0; k < LL_GMAX / 32; ++k)
+                raw[k] = lane + 32 * k < G ? ld_flagged(pres + lane + 32 * k) : 0ull;
+#pragma unroll
+            for (int k = 0; k < LL_GMAX / 32; ++k)
+                if (lane + 32 * k < G) flagged_take(raw[k], pres + lane + 32 * k, tag);
+        }
+    }
     for (int i = tid; i < EL; i += ST_CONS) {
         R.cnt[i] = 0;
         R.run[i] = 0;
@@ -369,8 +436,8 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
         if (warp == 0) {
             int e;
             float w, sg;
-            route_token<PER>(a, Ld, 0, R.idx, R.w, R.rinv, R.sgw, cta0, (st && lane == 0) ? st : nullptr, &e, &w,
-                             &sg);
+            route_token<PER, LLM>(a, Ld, 0, R.idx, R.w, R.rinv, R.sgw, cta0, (st && lane == 0) ? st : nullptr, &e,
+                                  &w, &sg, llg, ssq_l, tag);
             const int hs = Ld.sh_gate ? 1 : 0;
             const bool loc = lane < K && e >= a.lo && e < a.hi;
             const unsigned locs = __ballot_sync(0xffffffffu, loc);
@@ -415,7 +482,8 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
         return;
     } else {
         for (int t = warp; t < T; t += 8)
-            route_token<PER>(a, Ld, t, R.idx, R.w, R.rinv, R.sgw, cta0, (st && tid == 0) ? st : nullptr);
+            route_token<PER, LLM>(a, Ld, t, R.idx, R.w, R.rinv, R.sgw, cta0, (st && tid == 0) ? st : nullptr,
+                                  nullptr, nullptr, nullptr, llg, ssq_l, tag);
     }
     named_sync(BAR_CONS, ST_CONS);
     if (a.route_only) return;
@@ -1248,12 +1316,75 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                                 ? __ldcg(res + (size_t)(i / MOE_RT3) * H + (size_t)it3 * MOE_RT3 + i % MOE_RT3)
                                 : 0.0f;
                 }
-                // Rounds of RSU units whose chunks sit in distinct ring slots, with
-                // a consumer barrier between rounds: a slot's previous use is then
-                // finished before any warp waits on it again, so the parity wait
-                // below never looks two phases ahead.
+                // Every chunk of the tile in its own ring slot: the tile's
+                // nch x WS warp steps are split into 8 contiguous, equal ranges
+                // (a range spans at most a few chunks; each chunk's activation
+                // slice is loaded once per range).  The slots' previous uses all
+                // finished before the tile's last consumer barrier, so no wait
+                // looks two phases ahead.
+                if (nch <= NS_D) {
+                    const int S = nch * C::WS;
+                    const int s1 = (warp + 1) * S / 8;
+                    for (int s = warp * S / 8; s < s1;) {
+                        const int c = s / C::WS;
+                        const int wlo = s - c * C::WS;
+                        const int whi = s1 - c * C::WS < C::WS ? s1 - c * C::WS : C::WS;
+                        const int pos = dR.slot + c;
+                        const int slot = pos % NS_D;
+                        const unsigned par = (unsigned)(dR.phase ^ ((pos / NS_D) & 1));
+                        const uint8_t *st = dring + (size_t)slot * m.dslot;
+                        swait(dw + slot, par);
+                        swait(da + slot, par);
+                        if (stamp && s == 0 && it3 == bx) stamp_at(l, 7);
+                        const ChunkInfo ci = chunk_info(RT, c);
+                        const int16_t *aqs = reinterpret_cast<const int16_t *>(st + C::WB);
+                        const float *ass = reinterpret_cast<const float *>(st + C::WB + (size_t)TC * I * 2);
+                        for (int j = 0; j < ci.np; ++j) {
+                            const int t = RT.ptok[ci.p0 + j];
+                            const float wgt = RT.pw[ci.p0 + j];
+                            XSlice X[GI::CP];
+#pragma unroll
+                            for (int cp = 0; cp < GI::CP; ++cp)
+                                load_slice_q6k(X[cp], aqs + (size_t)j * I, ass + (size_t)j * (I / 32),
+                                               QK * (cp * 8 + bb) + 128 * (sub >> 1), sub & 1);
+                            // up to DB steps at a time: their dot chains and
+                            // shuffle reductions interleave
+                            constexpr int DB = C::WS < 4 ? C::WS : 4;
+                            for (int wb = wlo; wb < whi; wb += DB) {
+                                float v[DB];
+#pragma unroll
+                                for (int wi = 0; wi < DB; ++wi) {
+                                    v[wi] = 0.0f;
+                                    if (wb + wi < whi) {
+                                        const uint8_t *rowp =
+                                            st + (size_t)(wb + wi) * GI::STEPB + (size_t)rho * GI::ROWB;
+#pragma unroll
+                                        for (int cp = 0; cp < GI::CP; ++cp)
+                                            v[wi] += q6k_lane_dot(rowp + (size_t)(cp * 8 + bb) * Q6K_BYTES, sub >> 1,
+                                                                  sub & 1, L6, X[cp]);
+                                    }
+                                }
+#pragma unroll
+                                for (int o = GI::LPR / 2; o; o >>= 1)
+#pragma unroll
+                                    for (int wi = 0; wi < DB; ++wi) v[wi] += __shfl_xor_sync(0xffffffffu, v[wi], o);
+                                if (lr == 0)
+#pragma unroll
+                                    for (int wi = 0; wi < DB; ++wi)
+                                        if (wb + wi < whi) my_acc[t * MOE_RT3 + (wb + wi) * GI::RPW + rho] += wgt * v[wi];
+                            }
+                        }
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive_cnt(dempty + slot, (unsigned)(whi - wlo));
+                        s = c * C::WS + whi;
+                    }
+                }
+                // Otherwise rounds of RSU units whose chunks sit in distinct ring
+                // slots, with a consumer barrier between rounds: a slot's previous
+                // use is then finished before any warp waits on it again, so the
+                // parity wait below never looks two phases ahead.
                 const int RSU = 8 < NS_D * UPC ? 8 : NS_D * UPC;
-                for (int r0 = 0; r0 < nch * UPC; r0 += RSU) {
+                for (int r0 = 0; nch > NS_D && r0 < nch * UPC; r0 += RSU) {
                     const int u = r0 + warp;
                     if (warp >= RSU || u >= nch * UPC) {
                         named_sync(BAR_CONS, ST_CONS);

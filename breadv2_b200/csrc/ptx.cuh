@@ -123,6 +123,19 @@ __device__ __forceinline__ void red_release_sys(unsigned long long *p, unsigned 
 {
     asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+// Flagged exchange words: one 64-bit store / load at gpu scope (single-copy
+// atomic, served by L2), payload in the low and tag in the high 32 bits.
+__device__ __forceinline__ void st_flagged(unsigned long long *p, uint32_t payload, uint32_t tag)
+{
+    const unsigned long long w = ((unsigned long long)tag << 32) | payload;
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_flagged(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
+    return v;
+}
 __device__ __forceinline__ unsigned long long globaltimer()
 {
     unsigned long long t;
