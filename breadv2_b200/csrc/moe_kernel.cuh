@@ -37,6 +37,7 @@
 // every rank holds the same bits and routes identically.
 #pragma once
 #include <math.h>
+#include <stdlib.h>
 
 #include <mutex>
 
@@ -140,6 +141,41 @@ static __device__ __noinline__ uint32_t flagged_wait(const unsigned long long *p
 __device__ __forceinline__ uint32_t flagged_take(unsigned long long v, const unsigned long long *p, uint32_t tag)
 {
     return (uint32_t)(v >> 32) == tag ? (uint32_t)v : flagged_wait(p, tag);
+}
+// The words addr(k), k < N with bit k of `valid` set, polled as one batch --
+// every word still carrying an old tag is loaded again in the same round --
+// until all tags equal `tag` (bounded like flagged_wait).  r[k]: the words.
+template <int N, class Addr>
+__device__ __forceinline__ void flagged_poll(unsigned long long (&r)[N], unsigned valid, const Addr &addr, uint32_t tag)
+{
+#pragma unroll
+    for (int k = 0; k < N; ++k) r[k] = ((valid >> k) & 1u) ? ld_flagged(addr(k)) : 0ull;
+    unsigned pend = 0;
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+        if (((valid >> k) & 1u) && (uint32_t)(r[k] >> 32) != tag) pend |= 1u << k;
+    unsigned long long t0 = 0;
+    for (unsigned it = 0; pend; ++it) {
+        if (it > 2) __nanosleep(40);
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if ((pend >> k) & 1u) r[k] = ld_flagged(addr(k));
+        unsigned np = 0;
+#pragma unroll
+        for (int k = 0; k < N; ++k)
+            if (((pend >> k) & 1u) && (uint32_t)(r[k] >> 32) != tag) np |= 1u << k;
+        pend = np;
+        if (pend && (it & 31) == 31) {
+            if (dev_failed()) return;
+            const unsigned long long now = globaltimer();
+            if (!t0) {
+                t0 = now;
+            } else if (now - t0 > GRID_WAIT_NS) {
+                flag_error(DEVERR_TIMEOUT);
+                return;
+            }
+        }
+    }
 }
 
 // Grid-wide barrier number `idx` of this launch (all 256 consumer threads).
@@ -300,21 +336,18 @@ __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *
     float p[PER];
     float ss = 0.0f, score = 0.0f;
     if constexpr (LLM) {
+        // lane's logits e = lane + 32 j and, as entry PER, the score (row E)
         const unsigned long long *row = llg + (size_t)t * (E + 1);
-        unsigned long long raw[PER];
+        unsigned valid = Ld.w_sg ? 1u << PER : 0u;
 #pragma unroll
-        for (int j = 0; j < PER; ++j) {
-            const int e = lane + 32 * j;
-            raw[j] = e < E ? ld_flagged(row + e) : 0ull;
-        }
-        const unsigned long long rsc = Ld.w_sg ? ld_flagged(row + E) : 0ull;
+        for (int j = 0; j < PER; ++j)
+            if (lane + 32 * j < E) valid |= 1u << j;
+        unsigned long long raw[PER + 1];
+        flagged_poll(raw, valid, [&](int k) { return k < PER ? row + lane + 32 * k : row + E; }, tag);
         for (int g = lane; g < HG; g += 32) ss += ssq_l[t * HG + g];
 #pragma unroll
-        for (int j = 0; j < PER; ++j) {
-            const int e = lane + 32 * j;
-            p[j] = e < E ? __uint_as_float(flagged_take(raw[j], row + e, tag)) : -INFINITY;
-        }
-        if (Ld.w_sg) score = __uint_as_float(flagged_take(rsc, row + E, tag));
+        for (int j = 0; j < PER; ++j) p[j] = lane + 32 * j < E ? __uint_as_float((uint32_t)raw[j]) : -INFINITY;
+        if (Ld.w_sg) score = __uint_as_float((uint32_t)raw[PER]);
     } else {
 #pragma unroll
         for (int j = 0; j < PER; ++j) {
@@ -405,15 +438,14 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
     const int T = a.T, E = a.E, K = a.top_k;
     const int EL = a.hi - a.lo;
     if constexpr (LLM) {
-        if (warp == 0) {
+        if (warp == 0 && pres) {
             const int G = gridDim.x;
+            unsigned valid = 0;
+#pragma unroll
+            for (int k = 0; k < LL_GMAX / 32; ++k)
+                if (lane + 32 * k < G) valid |= 1u << k;
             unsigned long long raw[LL_GMAX / 32];
-#pragma unroll
-            for (int k = 0; k < LL_GMAX / 32; ++k)
-                raw[k] = lane + 32 * k < G ? ld_flagged(pres + lane + 32 * k) : 0ull;
-#pragma unroll
-            for (int k = 0; k < LL_GMAX / 32; ++k)
-                if (lane + 32 * k < G) flagged_take(raw[k], pres + lane + 32 * k, tag);
+            flagged_poll(raw, valid, [&](int k) { return pres + lane + 32 * k; }, tag);
         }
     }
     for (int i = tid; i < EL; i += ST_CONS) {
@@ -694,12 +726,19 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
 // ---------------------------------------------------------------------------
 // the step kernel
 // ---------------------------------------------------------------------------
-// BIG: more than ROUTER_TILE_T tokens (tiled router, shared ring arena, grid
-// routing above ROUTE_DIST_T); the decode instantiation carries none of that
-// code, which keeps its instruction footprint small.
-template <int NBH, int NBI, bool BIG>
+// MODE_BIG: more than ROUTER_TILE_T tokens (tiled router, shared ring arena,
+// grid routing above ROUTE_DIST_T).  MODE_SMALL: up to ROUTER_TILE_T tokens
+// with grid barriers (expert parallel, routing only).  MODE_LL: decode on one
+// GPU, up to LL_TMAX tokens, CTAs exchanging flagged words instead of meeting
+// at grid barriers (every CTA quantises the layer input itself).  Each
+// instantiation carries only its own paths, which keeps the decode
+// instruction footprint small.
+constexpr int MODE_LL = 0, MODE_SMALL = 1, MODE_BIG = 2;
+template <int NBH, int NBI, int MODE>
 __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_constant__ StepArgs a)
 {
+    constexpr bool BIG = MODE == MODE_BIG;
+    constexpr bool LL = MODE == MODE_LL;
     using C = SCfg<NBH, NBI>;
     using GH = typename C::GH;
     using GI = typename C::GI;
@@ -712,7 +751,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
     const int TC = T < MOE_TC ? T : MOE_TC;
     const int R = I / MOE_ROWTILE;  // gate/up row tiles per expert
     const int NT = H / MOE_RT3;     // 16-column tiles of h (down output)
-    const bool ep = a.ep_world > 1;
+    const bool ep = !LL && a.ep_world > 1;
     const bool norm = a.norm_eps >= 0.0f;
     const int NS_G = m.NS_G, NS_D = m.NS_D;
     const bool dist = BIG && T > ROUTE_DIST_T;        // routing spread over the grid (+1 barrier)
@@ -743,6 +782,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
     float *abuf = reinterpret_cast<float *>(smem + m.abuf);
     uint8_t *dring = smem + m.dring;
     float *acc = reinterpret_cast<float *>(smem + m.acc);
+    // flagged-exchange mode: this CTA's quantised copy of the layer input,
+    // the input itself (phase A) sharing bytes with the gathered intermediate
+    // (phase C), and the input's per-32 sums of squares
+    int16_t *xlq = reinterpret_cast<int16_t *>(smem + m.xloc);
+    float *xls = reinterpret_cast<float *>(smem + m.xloc + (size_t)T * H * 2);
+    float *xf = reinterpret_cast<float *>(smem + m.xf);
+    int16_t *alq = reinterpret_cast<int16_t *>(smem + m.xf);
+    float *als = reinterpret_cast<float *>(smem + m.xf + (size_t)T * (a.top_k + 1) * I * 2);
+    float *ssql = reinterpret_cast<float *>(smem + m.ssql);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + m.bars);
     uint64_t *rbar = bars;
     uint64_t *gfull = bars + 1, *gempty = gfull + NS_G;
@@ -769,6 +817,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
     for (int i = tid; i < 8 * T * MOE_RT3; i += ST_THREADS) acc[i] = 0.0f;
     __syncthreads();
     const unsigned long long epoch = __ldcg(a.ctrl + CTRL_EPOCH);
+    const unsigned long long seq0 = __ldcg(a.ctrl + CTRL_SEQ);
+    auto tag_of = [&](int l) { return (uint32_t)(seq0 + (unsigned long long)l + 1ull); };
+    auto par_of = [&](int l) { return (size_t)(l & 1); };
 
     if (warp == 8) {
         // ================================================================ producer
@@ -797,7 +848,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             }
             unsigned bytes = 0;
             for (int rl = 0; rl < m.RR; ++rl) {
-                const int r = bx * m.RR + rl;
+                const int r = bx + rl * G;
                 bytes += r < E ? H * 4 : (r == E && Ld.w_sg ? H * 2 : 0);
             }
             if (lane == 0) {
@@ -807,7 +858,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     mbar_arrive(rbar);
             }
             __syncwarp();
-            const int r = bx * m.RR + lane;
+            const int r = bx + lane * G;
             if (lane < m.RR) {
                 if (r < E)
                     bulk_g2s(rbuf + (size_t)lane * H, Ld.W_r + (size_t)r * H, H * 4, rbar);
@@ -857,18 +908,20 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             for (int it = bx; it < nch * R; it += G, ++nX) {
                 const int c = it / R, rt = it % R;  // R: a power of two
                 const ChunkInfo ci = chunk_info(RT, c);
-                const int xs_ = nX & 1;
-                if (lane == 0) {
-                    if (nX >= 2) swait(xempty + xs_, (unsigned)(((nX >> 1) - 1) & 1));
-                    mbar_arrive_expect_tx(xfull + xs_, (unsigned)(ci.np * C::XTOK));
-                }
-                __syncwarp();
-                if (lane < ci.np) {
-                    uint8_t *xb = xsl + (size_t)xs_ * m.xslot;
-                    const int t = RT.ptok[ci.p0 + lane];
-                    bulk_g2s(xb + (size_t)lane * H * 2, a.xq + (size_t)t * H, H * 2, xfull + xs_);
-                    bulk_g2s(xb + (size_t)TC * H * 2 + (size_t)lane * (H / 8), a.xs + (size_t)t * (H / 32), H / 8,
-                             xfull + xs_);
+                if constexpr (!LL) {  // (flagged mode: every CTA quantised the input itself)
+                    const int xs_ = nX & 1;
+                    if (lane == 0) {
+                        if (nX >= 2) swait(xempty + xs_, (unsigned)(((nX >> 1) - 1) & 1));
+                        mbar_arrive_expect_tx(xfull + xs_, (unsigned)(ci.np * C::XTOK));
+                    }
+                    __syncwarp();
+                    if (lane < ci.np) {
+                        uint8_t *xb = xsl + (size_t)xs_ * m.xslot;
+                        const int t = RT.ptok[ci.p0 + lane];
+                        bulk_g2s(xb + (size_t)lane * H * 2, a.xq + (size_t)t * H, H * 2, xfull + xs_);
+                        bulk_g2s(xb + (size_t)TC * H * 2 + (size_t)lane * (H / 8), a.xs + (size_t)t * (H / 32), H / 8,
+                                 xfull + xs_);
+                    }
                 }
                 const uint8_t *gb = mat_ptr(RT, Ld, a, ci.e, 0);
                 const uint8_t *ub = mat_ptr(RT, Ld, a, ci.e, 1);
@@ -929,20 +982,23 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             if (lane < dpre) issue_dw(dR.ahead(lane, NS_D), lane);
             __syncwarp();
             pstamp(l, 12);
-            // the intermediate of every CTA is complete after grid barrier (phase B)
-            if (lane == 0) {
-                const int bidx = l * nbl + (dist ? 2 : 1);
-                wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(bidx + 1) * G, false, GRID_WAIT_NS);
+            // the intermediate of every CTA is complete after grid barrier (phase
+            // B); flagged mode: the consumers gather it themselves
+            if constexpr (!LL) {
+                if (lane == 0) {
+                    const int bidx = l * nbl + (dist ? 2 : 1);
+                    wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(bidx + 1) * G, false, GRID_WAIT_NS);
+                }
+                __syncwarp();
+                fence_proxy_async_global();
             }
-            __syncwarp();
-            fence_proxy_async_global();
             pstamp(l, 14);
             for (int n0 = 0; n0 < nds; n0 += NS_D) {  // batches of distinct slots
                 const int nb = nds - n0 < NS_D ? nds - n0 : NS_D;
                 if (lane < nb) {
                     const Ring d = dR.ahead(lane, NS_D);
                     if (n0 + lane >= dpre) issue_dw(d, n0 + lane);
-                    issue_da(d, n0 + lane);
+                    if constexpr (!LL) issue_da(d, n0 + lane);
                 }
                 dR = dR.ahead(nb, NS_D);
                 __syncwarp();
@@ -973,13 +1029,16 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         }
         if (stamp) stamp_at(l, 0);
         const size_t TH = (size_t)a.ep_tmax * H;
+        const uint32_t tg = tag_of(l);
         auto xin = [&](size_t i) -> float {
+            if constexpr (LL) return xf[i];
             float v = __ldcg(src + i);
             if (pmb)
                 for (int r = 0; r < a.ep_world; ++r) v += __ldcg(pmb + (size_t)r * TH + i);
             return v;
         };
         auto xin4 = [&](size_t i) -> float4 {  // i: a multiple of 4
+            if constexpr (LL) return *reinterpret_cast<const float4 *>(xf + i);
             float4 v = __ldcg(reinterpret_cast<const float4 *>(src + i));
             if (pmb)
                 for (int r = 0; r < a.ep_world; ++r) {
@@ -991,8 +1050,40 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 }
             return v;
         };
-        // (1) this CTA's share of the int16 quantisation (+ group sums of squares)
-        {
+        if constexpr (LL) {
+            // (1) the whole layer input into shared memory: the caller's x for
+            // layer 0, else the previous layer's flagged output words
+            const int n = T * H;
+            if (l == 0) {
+                for (int i = 4 * tid; i < n; i += 4 * ST_CONS)
+                    *reinterpret_cast<float4 *>(xf + i) = __ldcg(reinterpret_cast<const float4 *>(src + i));
+            } else {
+                const unsigned long long *hin = a.ll_h + par_of(l - 1) * a.ll_h_n;
+                const uint32_t tgp = tag_of(l - 1);
+                for (int i0 = tid; i0 < n; i0 += 8 * ST_CONS) {
+                    unsigned valid = 0;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (i0 + k * ST_CONS < n) valid |= 1u << k;
+                    unsigned long long r[8];
+                    flagged_poll(r, valid, [&](int k) { return hin + i0 + k * ST_CONS; }, tgp);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if ((valid >> k) & 1u) xf[i0 + k * ST_CONS] = __uint_as_float((uint32_t)r[k]);
+                }
+            }
+            named_sync(BAR_CONS, ST_CONS);
+            // (2) all of it quantised to int16 per 32 (+ group sums of squares)
+            for (int gi = warp; gi < T * (H / 32); gi += 8) {
+                const float v = xf[gi * 32 + lane];
+                const float ss = warp_sum(v * v);
+                if (lane == 0) ssql[gi] = ss;
+                const int q = quant32(v, xls + gi, lane);
+                const int e = gi * 32 + lane, t = e / H;  // H: a power of two
+                xlq[(size_t)t * H + xq_pos(e - t * H)] = (int16_t)q;
+            }
+        } else {
+            // (1) this CTA's share of the int16 quantisation (+ group sums of squares)
             const int ngr = T * (H / 32);
             for (int gi = (G - 1 - bx) * 8 + warp; gi < ngr; gi += G * 8) {
                 const float v = xin((size_t)gi * 32 + lane);
@@ -1085,7 +1176,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             if (stamp) stamp_at(l, 18);
         } else {
             const int rl = warp / m.WPR, qt = warp % m.WPR;
-            const int row = bx * m.RR + rl;
+            const int row = bx + rl * G;
             const int nrows = E + (Ld.w_sg ? 1 : 0);
             const int seg = H / m.WPR, c0 = qt * seg;
             if (row < nrows) {
@@ -1147,19 +1238,25 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             if (stamp) stamp_at(l, 18);
             named_sync(BAR_CONS, ST_CONS);
             for (int i = tid; i < m.RR * T; i += ST_CONS) {
-                const int r_l = i / T, t = i % T, rr = bx * m.RR + r_l;
+                const int r_l = i / T, t = i % T, rr = bx + r_l * G;
                 if (rr < nrows) {
                     float v = 0.0f;
                     for (int q = 0; q < m.WPR; ++q) v += part[(r_l * m.WPR + q) * T + t];
-                    if (rr < E)
+                    if constexpr (LL)
+                        st_flagged(a.ll_lg + par_of(l) * a.ll_lg_n + (size_t)t * (E + 1) + rr, __float_as_uint(v), tg);
+                    else if (rr < E)
                         a.logits[(size_t)t * E + rr] = v;
                     else
                         a.score[t] = v;
                 }
             }
+            // flagged mode: this CTA is done with the layer input (and with
+            // everything of layer l-1).  With a router row in every CTA (rows
+            // r -> CTA r mod G) its logits say so; else its presence word does
+            if (LL && nrows < G && tid == 0) st_flagged(a.ll_pres + par_of(l) * a.ll_pres_n + bx, 0u, tg);
         }
         if (stamp) stamp_at(l, 1);
-        grid_barrier(a, bar++, tid);
+        if constexpr (!LL) grid_barrier(a, bar++, tid);
         if (stamp) stamp_at(l, 2);
 
         // ------------------------------------------------------------ phase B
@@ -1174,10 +1271,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             }
             grid_barrier(a, bar++, tid);
         }
-        if (E <= 256)
-            route_tables<8, BIG>(a, Ld, RT, l, bx == 0, st_l, dist);
-        else
-            route_tables<MOE_EMAX / 32, BIG>(a, Ld, RT, l, bx == 0, st_l, dist);
+        {
+            const unsigned long long *llg = LL ? a.ll_lg + par_of(l) * a.ll_lg_n : nullptr;
+            const unsigned long long *pres =
+                (LL && E + (Ld.w_sg ? 1 : 0) < G) ? a.ll_pres + par_of(l) * a.ll_pres_n : nullptr;
+            if (E <= 256)
+                route_tables<8, BIG, LL>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql, tg);
+            else
+                route_tables<MOE_EMAX / 32, BIG, LL>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql, tg);
+        }
         if (stamp) stamp_at(l, 3);
         named_sync(BAR_ALL, ST_THREADS);
         if (a.route_only) break;
@@ -1191,11 +1293,19 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 const int c = it / R, rt = it % R;  // R: a power of two
                 const ChunkInfo ci = chunk_info(RT, c);
                 const int xs_ = nX & 1;
-                swait(xfull + xs_, (unsigned)((nX >> 1) & 1));
+                if constexpr (!LL) swait(xfull + xs_, (unsigned)((nX >> 1) & 1));
                 if (stamp && it == bx) stamp_at(l, 4);
                 const uint8_t *xb = xsl + (size_t)xs_ * m.xslot;
-                const int16_t *xq = reinterpret_cast<const int16_t *>(xb);
-                const float *xsc = reinterpret_cast<const float *>(xb + (size_t)TC * H * 2);
+                // the chunk's token j (token t): its int16 activations and group
+                // scales (flagged mode: this CTA's own copy of every token)
+                auto xq_of = [&](int j, int t) -> const int16_t * {
+                    if constexpr (LL) return xlq + (size_t)t * H;
+                    return reinterpret_cast<const int16_t *>(xb) + (size_t)j * H;
+                };
+                auto xs_of = [&](int j, int t) -> const float * {
+                    if constexpr (LL) return xls + (size_t)t * (H / 32);
+                    return reinterpret_cast<const float *>(xb + (size_t)TC * H * 2) + (size_t)j * (H / 32);
+                };
                 if (C::SPI <= NS_G) {
                     // The item's sub-stages are in flight together: wait for all,
                     // then per token one activation slice feeds the item's
@@ -1211,8 +1321,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                             const float rsc = norm ? RT.rinv[t] : 1.0f;
 #pragma unroll
                             for (int cp = 0; cp < GH::CP; ++cp)
-                                load_slice_q4k(X[cp], xq + (size_t)j * H, xsc + (size_t)j * (H / 32),
-                                               QK * (cp * 8 + bb) + 64 * sub, rsc);
+                                load_slice_q4k(X[cp], xq_of(j, t), xs_of(j, t), QK * (cp * 8 + bb) + 64 * sub, rsc);
                         }
                         float gs[C::SPI], us[C::SPI];
 #pragma unroll
@@ -1257,8 +1366,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                                 const float rsc = norm ? RT.rinv[t] : 1.0f;
 #pragma unroll
                                 for (int cp = 0; cp < GH::CP; ++cp)
-                                    load_slice_q4k(X[cp], xq + (size_t)j * H, xsc + (size_t)j * (H / 32),
-                                                   QK * (cp * 8 + bb) + 64 * sub, rsc);
+                                    load_slice_q4k(X[cp], xq_of(j, t), xs_of(j, t), QK * (cp * 8 + bb) + 64 * sub, rsc);
                             }
                             float gs = 0.0f, us = 0.0f;
 #pragma unroll
@@ -1278,18 +1386,33 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     }
                 }
                 named_sync(BAR_CONS, ST_CONS);
-                if (lane == 0) mbar_arrive(xempty + xs_);
+                if (!LL && lane == 0) mbar_arrive(xempty + xs_);
                 for (int j = warp; j < ci.np; j += 8) {
                     const size_t p = (size_t)(ci.p0 + j);
-                    const int q = quant32(abuf[j * MOE_ROWTILE + lane], a.as + p * (I / 32) + rt, lane);
-                    a.aq[p * I + xq_pos(rt * MOE_ROWTILE + lane)] = (int16_t)q;
+                    if constexpr (LL) {
+                        // flagged words: two int16 (positions 2i, 2i+1 of the
+                        // xq_pos layout, one 8-value piece) per word, and the scale
+                        float sc;
+                        const int q = quant32(abuf[j * MOE_ROWTILE + lane], &sc, lane);
+                        const int qn = __shfl_down_sync(0xffffffffu, q, 1);
+                        const uint32_t tgl = tag_of(l);
+                        if (!(lane & 1))
+                            st_flagged(a.ll_a + par_of(l) * a.ll_a_n + p * (I / 2) +
+                                           (xq_pos(rt * MOE_ROWTILE + lane) >> 1),
+                                       ((uint32_t)q & 0xffffu) | ((uint32_t)qn << 16), tgl);
+                        if (lane == 0)
+                            st_flagged(a.ll_as + par_of(l) * a.ll_as_n + p * (I / 32) + rt, __float_as_uint(sc), tgl);
+                    } else {
+                        const int q = quant32(abuf[j * MOE_ROWTILE + lane], a.as + p * (I / 32) + rt, lane);
+                        a.aq[p * I + xq_pos(rt * MOE_ROWTILE + lane)] = (int16_t)q;
+                    }
                 }
                 named_sync(BAR_CONS, ST_CONS);
             }
         }
         if (stamp) stamp_at(l, 5);
         if (arena) fence_proxy_async_smem();  // the down copies reuse the gate/up stages' bytes
-        grid_barrier(a, bar++, tid);
+        if constexpr (!LL) grid_barrier(a, bar++, tid);
         if (stamp) stamp_at(l, 6);
 
         // ------------------------------------------------------------ phase C
@@ -1306,15 +1429,51 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             // unit's row dot products from it (independent chains).
             const int WG = (nch >= 8 || C::WS < 2) ? C::WS : C::WS / 2;
             const int UPC = C::WS / WG;
+            const uint32_t tg = tag_of(l);
+            if (LL && bx < NT) {
+                // flagged mode: gather the whole intermediate (every pair's
+                // int16 values and group scales) from the flagged words
+                const int P = RT.scal[2];
+                const unsigned long long *fa = a.ll_a + par_of(l) * a.ll_a_n;
+                const unsigned long long *fs = a.ll_as + par_of(l) * a.ll_as_n;
+                uint32_t *alq32 = reinterpret_cast<uint32_t *>(alq);
+                const int na = P * (I / 2), ns = P * (I / 32);
+                for (int i0 = tid; i0 < na + ns; i0 += 16 * ST_CONS) {
+                    unsigned valid = 0;
+#pragma unroll
+                    for (int k = 0; k < 16; ++k)
+                        if (i0 + k * ST_CONS < na + ns) valid |= 1u << k;
+                    unsigned long long r[16];
+                    flagged_poll(r, valid, [&](int k) {
+                        const int i = i0 + k * ST_CONS;
+                        return i < na ? fa + i : fs + (i - na);
+                    }, tg);
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        const int i = i0 + k * ST_CONS;
+                        if (i < na)
+                            alq32[i] = (uint32_t)r[k];
+                        else if (i < na + ns)
+                            als[i - na] = __uint_as_float((uint32_t)r[k]);
+                    }
+                }
+                named_sync(BAR_CONS, ST_CONS);
+            }
             for (int it3 = bx; it3 < NT; it3 += G) {
                 // residual of this tile's columns, loaded before the stages
+                // (flagged mode, l > 0: the previous layer's output words)
                 float rv[MOE_TMAX * MOE_RT3 / ST_CONS];
+                const unsigned long long *fres = (LL && l > 0) ? a.ll_h + par_of(l - 1) * a.ll_h_n : nullptr;
 #pragma unroll
                 for (int k = 0; k < MOE_TMAX * MOE_RT3 / ST_CONS; ++k) {
                     const int i = tid + k * ST_CONS;
-                    rv[k] = (!ep && i < T * MOE_RT3)
-                                ? __ldcg(res + (size_t)(i / MOE_RT3) * H + (size_t)it3 * MOE_RT3 + i % MOE_RT3)
-                                : 0.0f;
+                    const size_t o = (size_t)(i / MOE_RT3) * H + (size_t)it3 * MOE_RT3 + i % MOE_RT3;
+                    if (ep || i >= T * MOE_RT3)
+                        rv[k] = 0.0f;
+                    else if (fres)
+                        rv[k] = __uint_as_float(flagged_take(ld_flagged(fres + o), fres + o, tag_of(l - 1)));
+                    else
+                        rv[k] = __ldcg(res + o);
                 }
                 // Every chunk of the tile in its own ring slot: the tile's
                 // nch x WS warp steps are split into 8 contiguous, equal ranges
@@ -1334,11 +1493,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                         const unsigned par = (unsigned)(dR.phase ^ ((pos / NS_D) & 1));
                         const uint8_t *st = dring + (size_t)slot * m.dslot;
                         swait(dw + slot, par);
-                        swait(da + slot, par);
+                        if constexpr (!LL) swait(da + slot, par);
                         if (stamp && s == 0 && it3 == bx) stamp_at(l, 7);
                         const ChunkInfo ci = chunk_info(RT, c);
-                        const int16_t *aqs = reinterpret_cast<const int16_t *>(st + C::WB);
-                        const float *ass = reinterpret_cast<const float *>(st + C::WB + (size_t)TC * I * 2);
+                        const int16_t *aqs = LL ? alq + (size_t)ci.p0 * I : reinterpret_cast<const int16_t *>(st + C::WB);
+                        const float *ass = LL ? als + (size_t)ci.p0 * (I / 32)
+                                              : reinterpret_cast<const float *>(st + C::WB + (size_t)TC * I * 2);
                         for (int j = 0; j < ci.np; ++j) {
                             const int t = RT.ptok[ci.p0 + j];
                             const float wgt = RT.pw[ci.p0 + j];
@@ -1396,11 +1556,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     const unsigned par = (unsigned)(dR.phase ^ ((pos / NS_D) & 1));
                     const uint8_t *st = dring + (size_t)slot * m.dslot;
                     swait(dw + slot, par);
-                    swait(da + slot, par);
+                    if constexpr (!LL) swait(da + slot, par);
                     if (stamp && r0 == 0 && it3 == bx) stamp_at(l, 7);
                     const ChunkInfo ci = chunk_info(RT, c);
-                    const int16_t *aqs = reinterpret_cast<const int16_t *>(st + C::WB);
-                    const float *ass = reinterpret_cast<const float *>(st + C::WB + (size_t)TC * I * 2);
+                    const int16_t *aqs = LL ? alq + (size_t)ci.p0 * I : reinterpret_cast<const int16_t *>(st + C::WB);
+                    const float *ass = LL ? als + (size_t)ci.p0 * (I / 32)
+                                          : reinterpret_cast<const float *>(st + C::WB + (size_t)TC * I * 2);
                     for (int j = 0; j < ci.np; ++j) {
                         const int t = RT.ptok[ci.p0 + j];
                         const float wgt = RT.pw[ci.p0 + j];
@@ -1446,6 +1607,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                         // this rank's partial -> slot [slot_l][ep_rank] of every rank's mailbox (NVLink stores)
                         const size_t off = mb_slot_off(slot_l, a) + (size_t)a.ep_rank * TH + oi;
                         for (int p = 0; p < a.ep_world; ++p) a.ep_mb[p][off] = s;
+                    } else if (LL && l < a.L - 1) {
+                        st_flagged(a.ll_h + par_of(l) * a.ll_h_n + oi, __float_as_uint(rv[k] + s), tg);
                     } else {
                         out[oi] = rv[k] + s;
                     }
@@ -1463,7 +1626,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         }
         if (stamp) stamp_at(l, 8);
         if (arena) fence_proxy_async_smem();  // the next gate/up copies reuse the down stages' bytes
-        if (!ep) grid_barrier(a, bar++, tid);
+        if (!ep && !LL) grid_barrier(a, bar++, tid);
         if (stamp) stamp_at(l, 9);
     }
 
@@ -1493,6 +1656,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             a.ctrl[CTRL_GRID] = 0;
             a.ctrl[CTRL_EXIT] = 0;
             a.ctrl[CTRL_EPOCH] = epoch + 1;
+            a.ctrl[CTRL_SEQ] = seq0 + (unsigned long long)a.L;
             __threadfence();
         }
     }
@@ -1502,7 +1666,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
 // host side
 // ---------------------------------------------------------------------------
 template <int NBH, int NBI>
-static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G)
+static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G, int mode)
 {
     using C = SCfg<NBH, NBI>;
     size_t o = 0;
@@ -1518,7 +1682,8 @@ static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G)
     if (rr > 8) return -1;
     m.RR = rr;
     m.WPR = 8 / rr;
-    const bool arena = T > ROUTER_TILE_T;  // tiled router (no rows in smem), rings share one arena
+    const bool arena = mode == MODE_BIG;  // tiled router (no rows in smem), rings share one arena
+    const bool ll = mode == MODE_LL;
     m.rbuf = take(arena ? 16 : (size_t)rr * C::H * 4, 128);
     m.part = take((size_t)8 * T * 4, 16);
     const int GM = (EL < T * K ? EL : T * K) + 1, PM = T * (K + 1);
@@ -1539,23 +1704,41 @@ static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G)
     m.r_ptr = take((size_t)(EL > 0 ? EL : 1) * 3 * sizeof(void *), 16);
     m.r_chunk = take((size_t)(GM + (PM + MOE_TC - 1) / MOE_TC) * sizeof(int4), 16);
     const int TC = T < MOE_TC ? T : MOE_TC;
-    m.xslot = (uint32_t)al16((size_t)TC * C::XTOK);
-    m.xsl = take(2 * (size_t)m.xslot, 128);
+    if (ll) {
+        // no activation slots: every token quantised locally (xloc), the layer
+        // input (phase A) and the gathered intermediate (phase C) in one area
+        m.xslot = 0;
+        m.xsl = take(16, 128);
+        m.xloc = take((size_t)T * C::XTOK, 128);
+        const size_t xfb = (size_t)T * C::H * 4, alb = (size_t)T * (K + 1) * C::ATOK;
+        m.xf = take(xfb > alb ? xfb : alb, 128);
+        m.ssql = take((size_t)T * (C::H / 32) * 4, 16);
+    } else {
+        m.xslot = (uint32_t)al16((size_t)TC * C::XTOK);
+        m.xsl = take(2 * (size_t)m.xslot, 128);
+        m.xloc = m.xf = m.ssql = 0;
+    }
     m.abuf = take((size_t)TC * MOE_ROWTILE * 4, 16);
     m.acc = take((size_t)8 * T * MOE_RT3 * 4, 16);
-    m.dslot = (uint32_t)al16((size_t)C::WB + (size_t)TC * C::ATOK);
+    m.dslot = (uint32_t)al16((size_t)C::WB + (ll ? 0 : (size_t)TC * C::ATOK));
     const size_t bars_max = (size_t)(1 + 2 * 16 + 4 + 3 * 16) * 8 + 8;
     int nsg, nsd;
     if (!arena) {
         // few tokens: separate rings, so the down weights can be in flight
         // during the gate/up phase
-        nsg = 4;
-        while (nsg > 2 && (size_t)nsg * C::STB > 80 * 1024) --nsg;
+        // (flagged mode: fewer gate/up stages when the down ring would
+        // otherwise be shallow)
+        int nsg0 = 4;
+        while (nsg0 > 2 && (size_t)nsg0 * C::STB > 80 * 1024) --nsg0;
+        const size_t g0 = (o + 127) / 128 * 128;
+        for (nsg = nsg0;; --nsg) {
+            const size_t d0 = (g0 + (size_t)nsg * C::STB + 127) / 128 * 128;
+            const size_t avail = SMEM_LIMIT > d0 + bars_max ? SMEM_LIMIT - d0 - bars_max : 0;
+            nsd = (int)(avail / m.dslot);
+            if (nsd > 16) nsd = 16;
+            if (!ll || nsd >= 6 || nsg == 2) break;
+        }
         m.gring = take((size_t)nsg * C::STB, 128);
-        const size_t d0 = (o + 127) / 128 * 128;
-        const size_t avail = SMEM_LIMIT > d0 + bars_max ? SMEM_LIMIT - d0 - bars_max : 0;
-        nsd = (int)(avail / m.dslot);
-        if (nsd > 16) nsd = 16;
         m.dring = take((size_t)(nsd > 0 ? nsd : 0) * m.dslot, 128);
     } else {
         // many tokens: both rings in one arena (the down phase starts after
@@ -1590,8 +1773,10 @@ static int setup_nb()
     if (dev < 0 || dev >= MAX_DEVICES) return set_error(BREAD_ERR_STATE, "moe step: device %d", dev);
     std::lock_guard<std::mutex> lock(mu);
     if (!done[dev]) {
-        for (int big = 0; big < 2; ++big) {
-            auto kern = big ? moe_step_kernel<NBH, NBI, true> : moe_step_kernel<NBH, NBI, false>;
+        for (int mode = 0; mode < 3; ++mode) {
+            auto kern = mode == MODE_LL      ? moe_step_kernel<NBH, NBI, MODE_LL>
+                        : mode == MODE_SMALL ? moe_step_kernel<NBH, NBI, MODE_SMALL>
+                                             : moe_step_kernel<NBH, NBI, MODE_BIG>;
             BREAD_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LIMIT),
                        "moe step: shared-memory attribute");
             int n = 0;
@@ -1609,7 +1794,18 @@ static int launch_nb(StepArgs &a, cudaStream_t s)
 {
     BREAD_TRY(setup_nb<NBH, NBI>());
     const int G = sm_count();
-    if (step_layout<NBH, NBI>(a.sm, a.T, a.top_k, a.E, a.hi - a.lo, G))
+    // decode on one GPU: flagged-word exchange when its buffers are there and
+    // its layout fits (BREAD_NO_FLAGGED=1 forces the grid-barrier path)
+    static const bool no_flagged = [] {
+        const char *e = getenv("BREAD_NO_FLAGGED");
+        return e && e[0] == '1';
+    }();
+    int mode = a.T > ROUTER_TILE_T ? MODE_BIG : MODE_SMALL;
+    if (mode == MODE_SMALL && !no_flagged && a.ll_pres && a.ep_world == 1 && !a.route_only && a.T <= LL_TMAX &&
+        G <= LL_GMAX && (a.L == 1 || a.ll_h) &&
+        step_layout<NBH, NBI>(a.sm, a.T, a.top_k, a.E, a.hi - a.lo, G, MODE_LL) == 0)
+        mode = MODE_LL;
+    else if (step_layout<NBH, NBI>(a.sm, a.T, a.top_k, a.E, a.hi - a.lo, G, mode))
         return set_error(BREAD_ERR_ARG, "moe step: T=%d H=%d I=%d does not fit in shared memory", a.T, a.H, a.I);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);
@@ -1621,10 +1817,12 @@ static int launch_nb(StepArgs &a, cudaStream_t s)
     at[0].val.cooperative = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    if (a.T > ROUTER_TILE_T)
-        BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, true>, a), "moe step launch");
+    if (mode == MODE_BIG)
+        BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_BIG>, a), "moe step launch");
+    else if (mode == MODE_SMALL)
+        BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_SMALL>, a), "moe step launch");
     else
-        BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, false>, a), "moe step launch");
+        BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_LL>, a), "moe step launch");
     return BREAD_OK;
 }
 
