@@ -47,6 +47,7 @@ struct StepLayer {
     const float *W_r;                                // [E x H] fp32 router
     const __half *w_sg;                              // [H] fp16 shared-gate vector, or NULL
 };
+static_assert(sizeof(StepLayer) % 8 == 0, "layer descriptors are copied to shared memory in 8-byte words");
 
 // Control words at the head of the workspace (u64 each): the grid-barrier
 // counter, the exit ticket, the launch epoch and the layer sequence (tags of
@@ -75,10 +76,10 @@ constexpr int LL_GMAX = 256;  // CTAs of such a launch (presence words)
 // down stage landed, 8 down done, 9 layer end.  Producer: 10 routing tables
 // seen, 11 gate/up copies issued, 12 down weight copies issued, 13 next
 // layer's router rows issued, 14 gate/up barrier seen, 15 all down copies
-// issued.  Consumer thread 0 again: 16 quantisation share done, 17 router rows
-// landed, 18 router dots done, 19 routing inputs read, 20 top-k done, 21
-// tables built (= 3 before the chunk table), 22 down stages done, 23 down
-// columns stored.
+// issued.  Consumer thread 0 again: 16 quantisation share done (flagged
+// mode: layer input read), 17 router rows landed, 18 router dots done, 19
+// routing inputs read, 20 top-k done, 21 tables built (= 3 before the chunk
+// table), 22 down stages done, 23 down columns stored.
 constexpr int STAMPS = 24;
 constexpr size_t CTRL_BYTES = 256;
 
@@ -138,6 +139,7 @@ struct StepWs {
 struct StepSmem {
     uint32_t rbuf, part, xsl, gring, abuf, dring, acc, bars, total;
     uint32_t xloc, xf, ssql;  // flagged-exchange mode: quantised tokens, layer input / intermediate, group sums
+    uint32_t ldesc;           // copies of the L layer descriptors (StepArgs::layers)
     uint32_t r_idx, r_w, r_rinv, r_sgw, r_cnt, r_run, r_off, r_gexp, r_goff, r_gcnt, r_gcpre, r_ptok, r_pw, r_scal, r_ptr, r_chunk;
     uint32_t xslot, dslot;
     int NS_G, NS_D, RR, WPR;

@@ -191,7 +191,14 @@ __device__ __forceinline__ void grid_barrier(const StepArgs &a, int idx, int tid
     named_sync(BAR_CONS, ST_CONS);
 }
 
-__device__ __forceinline__ StepLayer layer_desc(const StepArgs &a, int l) { return a.layers ? a.layers[l] : a.l0; }
+// Layer l's descriptor: the kernel's shared-memory copy of StepArgs::layers
+// (made at launch: a global load here would sit right after each layer's
+// routing, on the critical path), else l0.
+__device__ __forceinline__ StepLayer layer_desc(const StepArgs &a, int l)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    return a.layers ? reinterpret_cast<const StepLayer *>(smem + a.sm.ldesc)[l] : a.l0;
+}
 __device__ __forceinline__ const float *in_of(const StepArgs &a, int l) { return l == 0 ? a.x : a.buf[l & 1]; }
 __device__ __forceinline__ float *out_of(const StepArgs &a, int l) { return l == a.L - 1 ? a.y : a.buf[(l + 1) & 1]; }
 
@@ -815,6 +822,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         fence_mbar_init();
     }
     for (int i = tid; i < 8 * T * MOE_RT3; i += ST_THREADS) acc[i] = 0.0f;
+    if (a.layers) {
+        const unsigned long long *src = reinterpret_cast<const unsigned long long *>(a.layers);
+        unsigned long long *dst = reinterpret_cast<unsigned long long *>(smem + m.ldesc);
+        for (int i = tid; i < a.L * (int)(sizeof(StepLayer) / 8); i += ST_THREADS) dst[i] = __ldg(src + i);
+    }
     __syncthreads();
     const unsigned long long epoch = __ldcg(a.ctrl + CTRL_EPOCH);
     const unsigned long long seq0 = __ldcg(a.ctrl + CTRL_SEQ);
@@ -901,7 +913,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             if (a.route_only) break;
             pstamp(l, 10);
             const StepLayer Ld = layer_desc(a, l);
-            fence_proxy_async_global();
+            // (the copies below read data other CTAs wrote only in barrier modes)
+            if constexpr (!LL) fence_proxy_async_global();
             const int nch = RT.scal[1];
             // gate/up items (chunk c, row tile rt): activations of the chunk's
             // tokens + 32 gate and up rows in sub-stages
@@ -1073,15 +1086,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 }
             }
             named_sync(BAR_CONS, ST_CONS);
-            // (2) all of it quantised to int16 per 32 (+ group sums of squares)
-            for (int gi = warp; gi < T * (H / 32); gi += 8) {
-                const float v = xf[gi * 32 + lane];
-                const float ss = warp_sum(v * v);
-                if (lane == 0) ssql[gi] = ss;
-                const int q = quant32(v, xls + gi, lane);
-                const int e = gi * 32 + lane, t = e / H;  // H: a power of two
-                xlq[(size_t)t * H + xq_pos(e - t * H)] = (int16_t)q;
-            }
+            // (quantised after the router rows, below)
         } else {
             // (1) this CTA's share of the int16 quantisation (+ group sums of squares)
             const int ngr = T * (H / 32);
@@ -1254,6 +1259,20 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             // everything of layer l-1).  With a router row in every CTA (rows
             // r -> CTA r mod G) its logits say so; else its presence word does
             if (LL && nrows < G && tid == 0) st_flagged(a.ll_pres + par_of(l) * a.ll_pres_n + bx, 0u, tg);
+        }
+        if constexpr (LL) {
+            // the whole input quantised to int16 per 32 (+ group sums of
+            // squares), after the logits are out: it overlaps the wait for the
+            // other CTAs' logits instead of delaying them
+            for (int gi = warp; gi < T * (H / 32); gi += 8) {
+                const float v = xf[gi * 32 + lane];
+                const float ss = warp_sum(v * v);
+                if (lane == 0) ssql[gi] = ss;
+                const int q = quant32(v, xls + gi, lane);
+                const int e = gi * 32 + lane, t = e / H;  // H: a power of two
+                xlq[(size_t)t * H + xq_pos(e - t * H)] = (int16_t)q;
+            }
+            named_sync(BAR_CONS, ST_CONS);  // group sums and int16 values complete before routing
         }
         if (stamp) stamp_at(l, 1);
         if constexpr (!LL) grid_barrier(a, bar++, tid);
@@ -1666,7 +1685,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
 // host side
 // ---------------------------------------------------------------------------
 template <int NBH, int NBI>
-static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G, int mode)
+static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G, int mode, int ndesc)
 {
     using C = SCfg<NBH, NBI>;
     size_t o = 0;
@@ -1682,6 +1701,7 @@ static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G, int mode
     if (rr > 8) return -1;
     m.RR = rr;
     m.WPR = 8 / rr;
+    m.ldesc = take((size_t)ndesc * sizeof(StepLayer), 16);
     const bool arena = mode == MODE_BIG;  // tiled router (no rows in smem), rings share one arena
     const bool ll = mode == MODE_LL;
     m.rbuf = take(arena ? 16 : (size_t)rr * C::H * 4, 128);
@@ -1801,11 +1821,12 @@ static int launch_nb(StepArgs &a, cudaStream_t s)
         return e && e[0] == '1';
     }();
     int mode = a.T > ROUTER_TILE_T ? MODE_BIG : MODE_SMALL;
+    const int ndesc = a.layers ? a.L : 0;
     if (mode == MODE_SMALL && !no_flagged && a.ll_pres && a.ep_world == 1 && !a.route_only && a.T <= LL_TMAX &&
         G <= LL_GMAX && (a.L == 1 || a.ll_h) &&
-        step_layout<NBH, NBI>(a.sm, a.T, a.top_k, a.E, a.hi - a.lo, G, MODE_LL) == 0)
+        step_layout<NBH, NBI>(a.sm, a.T, a.top_k, a.E, a.hi - a.lo, G, MODE_LL, ndesc) == 0)
         mode = MODE_LL;
-    else if (step_layout<NBH, NBI>(a.sm, a.T, a.top_k, a.E, a.hi - a.lo, G, mode))
+    else if (step_layout<NBH, NBI>(a.sm, a.T, a.top_k, a.E, a.hi - a.lo, G, mode, ndesc))
         return set_error(BREAD_ERR_ARG, "moe step: T=%d H=%d I=%d does not fit in shared memory", a.T, a.H, a.I);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);
