@@ -1086,7 +1086,28 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 }
             }
             named_sync(BAR_CONS, ST_CONS);
-            // (quantised after the router rows, below)
+            // (2) per-32 sums of squares (all that routing needs), four groups
+            // at a time so their reductions interleave; the int16 quantisation
+            // follows the router rows, below.  (Published to the routing warps
+            // by the consumer barrier after the router dots.)
+            const int ngr = T * (H / 32);
+            for (int g0 = warp; g0 < ngr; g0 += 32) {
+                float v[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int gi = g0 + 8 * k;
+                    const float x = gi < ngr ? xf[gi * 32 + lane] : 0.0f;
+                    v[k] = x * x;
+                }
+#pragma unroll
+                for (int o = 16; o; o >>= 1)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) v[k] += __shfl_xor_sync(0xffffffffu, v[k], o);
+                if (lane == 0)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (g0 + 8 * k < ngr) ssql[g0 + 8 * k] = v[k];
+            }
         } else {
             // (1) this CTA's share of the int16 quantisation (+ group sums of squares)
             const int ngr = T * (H / 32);
@@ -1261,18 +1282,16 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             if (LL && nrows < G && tid == 0) st_flagged(a.ll_pres + par_of(l) * a.ll_pres_n + bx, 0u, tg);
         }
         if constexpr (LL) {
-            // the whole input quantised to int16 per 32 (+ group sums of
-            // squares), after the logits are out: it overlaps the wait for the
-            // other CTAs' logits instead of delaying them
-            for (int gi = warp; gi < T * (H / 32); gi += 8) {
-                const float v = xf[gi * 32 + lane];
-                const float ss = warp_sum(v * v);
-                if (lane == 0) ssql[gi] = ss;
-                const int q = quant32(v, xls + gi, lane);
+            // the whole input quantised to int16 per 32, after the logits are
+            // out: it overlaps the wait for the other CTAs' logits.  One token:
+            // warp 0 routes meanwhile (warps 1..7 quantise); the routing's
+            // consumer barriers publish the values before any gate/up item.
+            const int w0 = T == 1 ? 1 : 0, nw = 8 - w0;
+            for (int gi = warp - w0; warp >= w0 && gi < T * (H / 32); gi += nw) {
+                const int q = quant32(xf[gi * 32 + lane], xls + gi, lane);
                 const int e = gi * 32 + lane, t = e / H;  // H: a power of two
                 xlq[(size_t)t * H + xq_pos(e - t * H)] = (int16_t)q;
             }
-            named_sync(BAR_CONS, ST_CONS);  // group sums and int16 values complete before routing
         }
         if (stamp) stamp_at(l, 1);
         if constexpr (!LL) grid_barrier(a, bar++, tid);
