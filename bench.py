@@ -134,6 +134,24 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU side: the reference's own CPU path (oracle/_ref) or the oracle port
 # ---------------------------------------------------------------------------
+def host_info() -> dict:
+    """Logical cores this process may use and the CPU model of the host."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"host_cores": n, "cpu_model": model}
+
+
 class CpuLayerSampler:
     """Runs whole MoE layers of the benchmark stack on the host with the
     reference's CPU code: route_layer's arithmetic (one_layer.cu:937-992) and the
@@ -143,10 +161,12 @@ class CpuLayerSampler:
     def __init__(self, seed: int, threads: int):
         import numpy as np
 
-        import breadv2_b200 as bb
         import oracle
 
-        self.np, self.bb, self.oracle = np, bb, oracle
+        # inputs from the oracle's host restatement of the seeded generator
+        # (the same bytes as the product library's), so this CPU leg loads no
+        # product code
+        self.np, self.oracle = np, oracle
         self.kind = "reference" if oracle.ref_available() else "port"
         self.seed, self.threads = seed, threads
         self.cache = {}
@@ -157,13 +177,13 @@ class CpuLayerSampler:
     def _blocks(self, layer, kind, e, n, qt):
         key = (layer, kind, e)
         if key not in self.cache:
-            self.cache[key] = self.bb.synth_blocks_host(n, qt, self.seed, self._sid(layer, kind, e))
+            self.cache[key] = self.oracle.synth_blocks(n, qt, self.seed, self._sid(layer, kind, e))
         return self.cache[key]
 
     def layer_inputs(self, layer):
-        bb = self.bb
-        W = bb.synth_normal_host(E * H, 0.02, self.seed, self._sid(layer, 6, 0)).reshape(E, H)
-        sg = bb.synth_normal_host(H, 0.02, self.seed, self._sid(layer, 7, 0), half=True)
+        o = self.oracle
+        W = o.synth_normal(E * H, 0.02, self.seed, self._sid(layer, 6, 0)).reshape(E, H)
+        sg = o.synth_normal(H, 0.02, self.seed, self._sid(layer, 7, 0), half=True)
         return W, sg
 
     def run_layer(self, layer, h, W, sg):
@@ -198,12 +218,10 @@ class CpuLayerSampler:
 def cpu_sample(T: int, seed: int, threads: int, budget_s: float = 15.0):
     """Time whole reference-CPU layers until ~budget_s of CPU work; returns
     (tok/s for the 40-layer stack, layers timed, kind)."""
-    import numpy as np
-
-    import breadv2_b200 as bb
+    import oracle
 
     s = CpuLayerSampler(seed, threads)
-    h = bb.synth_normal_host(T * H, 1.0, seed, 777).reshape(T, H)
+    h = oracle.synth_normal(T * H, 1.0, seed, 777).reshape(T, H)
     spent, layers = 0.0, 0
     while layers < LAYERS and (layers == 0 or spent < budget_s):
         W, sg = s.layer_inputs(layers)
@@ -219,14 +237,12 @@ def run_reference(args, rank: int, world: int) -> int:
     host cores, same metric and config; rank 0 only."""
     if rank != 0:
         return 0
-    import numpy as np
+    import oracle
 
-    import breadv2_b200 as bb
-
-    threads = os.cpu_count() or 1
+    threads = host_info()["host_cores"]
     s = CpuLayerSampler(args.seed, threads)
     T = args.batch
-    hs = [bb.synth_normal_host(T * H, 1.0, args.seed, 900 + i).reshape(T, H) for i in range(N_INPUTS)]
+    hs = [oracle.synth_normal(T * H, 1.0, args.seed, 900 + i).reshape(T, H) for i in range(N_INPUTS)]
     times = []
     for i in range(args.warmup + args.steps):
         layer = i % LAYERS
@@ -242,7 +258,8 @@ def run_reference(args, rank: int, world: int) -> int:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * LAYERS * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_block(args, world),
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": s.kind, "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": s.kind, "sample": sample,
+                         "threads": threads, **host_info()},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -423,9 +440,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        threads = min(8, os.cpu_count() or 1)
+        threads = min(8, host_info()["host_cores"])
         v, layers, kind, per_layer = cpu_sample(T, args.seed, threads)
-        cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": kind,
+        cpu = {"value": v, "unit": "tok/s", "cores": threads, "threads": threads, **host_info(), "kind": kind,
                "sample": f"{layers} of 40 MoE layers at T={T} on the host ({per_layer * 1e3:.1f} ms/layer, "
                          f"OpenMP over experts as expert_bench.cu:158-179); tok/s = T / (40 x layer time)"}
 

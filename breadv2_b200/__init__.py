@@ -61,6 +61,24 @@ def matvec_f32(w, x, rows: int, cols: int, qtype: int, y=None, stream=None):
     return y
 
 
+def lm_head_argmax(w, x, rows: int, cols: int, qtype: int, round_half: bool = True, state=None, logits=None,
+                   stream=None):
+    """Greedy token of the head GEMV W x on the device (compute_logits +
+    greedy_sample of main.cu:297-337): returns (token int32[1], value fp32[1])
+    device tensors.  `state`: a reusable zeroed int64[2] device tensor."""
+    import torch
+
+    dev = x.device
+    if state is None:
+        state = torch.zeros(2, dtype=torch.int64, device=dev)
+    token = torch.empty(1, dtype=torch.int32, device=dev)
+    value = torch.empty(1, dtype=torch.float32, device=dev)
+    check(lib().bread_lm_head_argmax(_p(w), _p(x), rows, cols, qtype, int(round_half),
+                                     _p(logits) if logits is not None else None, _p(token), _p(value), _p(state),
+                                     _s(stream)), "bread_lm_head_argmax")
+    return token, value
+
+
 def dequant(w, n_blocks: int, qtype: int, out=None, stream=None):
     """Bit-exact dequantisation (layer_ops.cu:44-105) of n_blocks blocks to fp32."""
     if out is None:
@@ -255,6 +273,22 @@ class ExpertStack:
         check(lib().bread_stack_routing_stats(self.handle, g.ctypes.data_as(ctypes.c_void_p),
                                               p.ctypes.data_as(ctypes.c_void_p)), "bread_stack_routing_stats")
         return g, p
+
+    def routing(self):
+        """Routing of every layer of the last step as the kernel ran it:
+        (idx [L, T, K] int32, w [L, T, K] fp32, sg_weight [L, T] fp32)."""
+        import numpy as np
+
+        L, K, Tm = self.cfg.n_layers, self.cfg.top_k, self.cfg.max_tokens
+        idx = np.zeros(L * Tm * K, dtype=np.int32)
+        w = np.zeros(L * Tm * K, dtype=np.float32)
+        sg = np.zeros(L * Tm, dtype=np.float32)
+        T = ctypes.c_int(0)
+        check(lib().bread_stack_routing(self.handle, idx.ctypes.data_as(ctypes.c_void_p),
+                                        w.ctypes.data_as(ctypes.c_void_p), sg.ctypes.data_as(ctypes.c_void_p),
+                                        ctypes.byref(T)), "bread_stack_routing")
+        T = T.value
+        return (idx[: L * T * K].reshape(L, T, K), w[: L * T * K].reshape(L, T, K), sg[: L * T].reshape(L, T))
 
     def step_host(self, h_in, h_out, stream=None) -> None:
         """h_in/h_out: [T, hidden] fp32 host tensors (pinned for speed)."""

@@ -27,6 +27,7 @@ SIGNATURES = {
     "bread_matvec_f32": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "bread_matvec_batch_f32": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "bread_dequant": (_I, [_P, _P, _LL, _I, _P]),
+    "bread_lm_head_argmax": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "bread_rmsnorm_half_c": (_I, [_P, _P, _I, _F, _P]),
     "bread_silu_mul_c": (_I, [_P, _P, _I, _P]),
     "bread_scale_accum_c": (_I, [_P, _P, _F, _I, _P]),
@@ -50,6 +51,7 @@ SIGNATURES = {
     "bread_stack_profile_step": (_I, [_P, _P, _I, _P, _P]),
     "bread_stack_profile_stamps": (_I, [_P, _P, _SZ, ctypes.POINTER(_I)]),
     "bread_stack_routing_stats": (_I, [_P, _P, _P]),
+    "bread_stack_routing": (_I, [_P, _P, _P, _P, ctypes.POINTER(_I)]),
     "bread_synth_blocks": (_I, [_P, _LL, _I, _U64, _U64, _P]),
     "bread_synth_normal_f32": (_I, [_P, _LL, _F, _U64, _U64, _P]),
     "bread_synth_normal_f16": (_I, [_P, _LL, _F, _U64, _U64, _P]),

@@ -3,6 +3,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -28,15 +30,17 @@ int cuda_status(cudaError_t e, const char *what)
 
 int sm_count()
 {
-    static int cached[64] = {0};
+    // per-device cache; atomics because host threads may make their first
+    // calls at the same time (both would store the same value)
+    static std::atomic<int> cached[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (!cached[dev]) {
-        int n = 0;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (!n) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        cached[dev] = n;
+        cached[dev].store(n, std::memory_order_relaxed);
     }
-    return cached[dev];
+    return n;
 }
 
 }  // namespace bread

@@ -81,10 +81,58 @@ __device__ __forceinline__ void quantise_to_smem(const void *x, int T, int cols,
     }
 }
 
-template <int QT, int NB, bool ONE_TOKEN, bool IN_HALF, bool OUT_HALF>
+// Fused greedy sampling (the argmax after the lm-head GEMV that
+// greedy_sample, main.cu:324-337, runs on the host over fp16 logits): every
+// lane that finishes a row folds it into a running 64-bit key
+// {order-preserving value bits, ~row}, so the largest value wins and, among
+// equal values, the lowest row (the reference's strict `>` scan).  Each warp
+// then posts its best key with one atomicMax; the last warp to arrive (ticket)
+// decodes the winner into token/value and re-zeroes the state for the next
+// call.  NaN logits never win (the reference's `v > best` skips them).
+struct ArgmaxArgs {
+    unsigned long long *key;  // state[0]; state[1] low word: arrival ticket
+    unsigned *ticket;
+    int *token;
+    float *value;
+    int round_half;           // 1: compare fp16-rounded logits (what greedy_sample sees)
+    int finalize;             // 0: another launch arrives after this one and finalises
+};
+__device__ __forceinline__ unsigned long long am_key(float v, long long row, int round_half)
+{
+    if (round_half) v = __half2float(__float2half_rn(v));
+    if (v != v) return 0ull;
+    const uint32_t b = __float_as_uint(v);
+    const uint32_t k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)k << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)row);
+}
+// One warp's arrival (all 32 lanes, each with its best key); n_arrive: warps
+// of this launch.
+__device__ __forceinline__ void am_arrive(const ArgmaxArgs &am, unsigned long long best, unsigned n_arrive)
+{
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) {
+        if (best) atomicMax(am.key, best);
+        __threadfence();
+        if (am.finalize && atomicAdd(am.ticket, 1u) == n_arrive - 1) {
+            __threadfence();
+            const unsigned long long k = atomicExch(am.key, 0ull);
+            atomicExch(am.ticket, 0u);
+            const uint32_t kv = (uint32_t)(k >> 32);
+            const uint32_t b = (kv & 0x80000000u) ? (kv & 0x7FFFFFFFu) : ~kv;
+            *am.token = k ? (int)(0xFFFFFFFFu - (uint32_t)k) : 0;
+            if (am.value) *am.value = k ? __uint_as_float(b) : __int_as_float(0x7fc00000);
+        }
+    }
+}
+
+template <int QT, int NB, bool ONE_TOKEN, bool IN_HALF, bool OUT_HALF, bool AM = false>
 __global__ void __launch_bounds__(GEMV_WARPS * 32)
 gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__restrict__ x, int T,
-                void *__restrict__ y, int rows_total)
+                void *__restrict__ y, int rows_total, const ArgmaxArgs am)
 {
     using G = Geo<QT, NB>;
     constexpr size_t CHUNK = GemvSmem<QT, NB>::chunk;
@@ -154,6 +202,7 @@ gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__r
         for (int cp = 0; cp < G::CP; ++cp) slice_of(X1[cp], 0, cp);
     }
 
+    unsigned long long best = 0ull;  // AM: this lane's best key
     for (int c = 0; c < nchunks; ++c) {
         const int slot = c % GEMV_STAGES;
         if (!mbar_wait(my_bar + slot, (unsigned)((c / GEMV_STAGES) & 1))) return;
@@ -201,10 +250,15 @@ gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__r
                     for (int o = G::LPR / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                     if (lr == 0) {
                         const size_t oi = (size_t)t * rows_total + row;
-                        if (OUT_HALF)
+                        if (AM) {
+                            const unsigned long long k = am_key(v, row, am.round_half);
+                            best = k > best ? k : best;
+                            if (y) reinterpret_cast<float *>(y)[oi] = v;
+                        } else if (OUT_HALF) {
                             reinterpret_cast<__half *>(y)[oi] = __float2half_rn(v);
-                        else
+                        } else {
                             reinterpret_cast<float *>(y)[oi] = v;
+                        }
                     }
                 }
             }
@@ -215,18 +269,20 @@ gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__r
             issue(c + GEMV_STAGES);
         }
     }
+    if (AM) am_arrive(am, best, gridDim.x * GEMV_WARPS);
 }
 
 // One warp per row; exact element dequantisation; any alignment.
-template <int QT, bool IN_HALF, bool OUT_HALF>
+template <int QT, bool IN_HALF, bool OUT_HALF, bool AM = false>
 __global__ void gemv_generic_kernel(const uint8_t *__restrict__ W, int row0, int rows, int cols, const void *x, int T,
-                                    void *y, int rows_total)
+                                    void *y, int rows_total, const ArgmaxArgs am)
 {
     constexpr int BE = QT == BREAD_QTYPE_Q8_0 ? Q80_ELEMS : QK;
     constexpr int BBY = QT == BREAD_QTYPE_Q4_K ? Q4K_BYTES : QT == BREAD_QTYPE_Q6_K ? Q6K_BYTES : Q80_BYTES;
     const int lane = threadIdx.x & 31;
     const int wpb = blockDim.x >> 5;
     const int nb = cols / BE;
+    unsigned long long best = 0ull;  // AM: lane 0's best key
     for (int r = blockIdx.x * wpb + (threadIdx.x >> 5); r < rows; r += gridDim.x * wpb) {
         const int row = row0 + r;
         const uint8_t *rp = W + (size_t)row * nb * BBY;
@@ -243,13 +299,19 @@ __global__ void gemv_generic_kernel(const uint8_t *__restrict__ W, int row0, int
             for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
             if (lane == 0) {
                 const size_t oi = (size_t)t * rows_total + row;
-                if (OUT_HALF)
+                if (AM) {
+                    const unsigned long long k = am_key(acc, row, am.round_half);
+                    best = k > best ? k : best;
+                    if (y) reinterpret_cast<float *>(y)[oi] = acc;
+                } else if (OUT_HALF) {
                     reinterpret_cast<__half *>(y)[oi] = __float2half_rn(acc);
-                else
+                } else {
                     reinterpret_cast<float *>(y)[oi] = acc;
+                }
             }
         }
     }
+    if (AM) am_arrive(am, best, gridDim.x * wpb);
 }
 
 // Bit-exact block dequantisation: one warp per block.
@@ -269,11 +331,11 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ W, float *__restrict_
 // ---------------------------------------------------------------------------
 // host dispatch
 // ---------------------------------------------------------------------------
-template <int QT, int NB, bool ONE, bool IH, bool OH>
+template <int QT, int NB, bool ONE, bool IH, bool OH, bool AM = false>
 static int launch_fast(const uint8_t *W, long long nsteps, const void *x, int T, void *y, int rows_total,
-                       cudaStream_t stream)
+                       cudaStream_t stream, const ArgmaxArgs &am = ArgmaxArgs{})
 {
-    auto kern = gemv_tma_kernel<QT, NB, ONE, IH, OH>;
+    auto kern = gemv_tma_kernel<QT, NB, ONE, IH, OH, AM>;
     const size_t smem = GemvSmem<QT, NB>::bytes(T);
     static int per_sm = 0;  // per instantiation; the attribute covers the largest T
     if (!per_sm) {
@@ -289,42 +351,47 @@ static int launch_fast(const uint8_t *W, long long nsteps, const void *x, int T,
     const long long want = (nsteps + GEMV_WARPS - 1) / GEMV_WARPS;
     const long long cap = (long long)sm_count() * per_sm;
     const int grid = (int)(want < cap ? want : cap);
-    kern<<<grid, GEMV_WARPS * 32, smem, stream>>>(W, nsteps, x, T, y, rows_total);
+    kern<<<grid, GEMV_WARPS * 32, smem, stream>>>(W, nsteps, x, T, y, rows_total, am);
     BREAD_CUDA(cudaGetLastError(), "gemv fast launch");
     return BREAD_OK;
 }
 
-template <int QT, bool IH, bool OH>
+template <int QT, bool IH, bool OH, bool AM = false>
 static int launch_generic(const uint8_t *W, int row0, int rows, int cols, const void *x, int T, void *y,
-                          int rows_total, cudaStream_t stream)
+                          int rows_total, cudaStream_t stream, const ArgmaxArgs &am = ArgmaxArgs{})
 {
     if (rows <= 0) return BREAD_OK;
     const int warps = 8;
     long long want = ((long long)rows + warps - 1) / warps;
     const long long cap = (long long)sm_count() * 8;
     const int grid = (int)(want < cap ? want : cap);
-    gemv_generic_kernel<QT, IH, OH><<<grid, warps * 32, 0, stream>>>(W, row0, rows, cols, x, T, y, rows_total);
+    gemv_generic_kernel<QT, IH, OH, AM><<<grid, warps * 32, 0, stream>>>(W, row0, rows, cols, x, T, y, rows_total, am);
     BREAD_CUDA(cudaGetLastError(), "gemv generic launch");
     return BREAD_OK;
 }
 
-template <int QT, bool IH, bool OH>
-static int gemv_dispatch_q(const uint8_t *W, int rows, int cols, const void *x, int T, void *y, cudaStream_t stream)
+// AM (argmax, one fp32 token): the launch that runs last finalises.
+template <int QT, bool IH, bool OH, bool AM = false>
+static int gemv_dispatch_q(const uint8_t *W, int rows, int cols, const void *x, int T, void *y, cudaStream_t stream,
+                           const ArgmaxArgs &am = ArgmaxArgs{})
 {
     const int nb = cols / QK;
     const bool aligned = (reinterpret_cast<uintptr_t>(W) & 15) == 0;
     int rpw = 0;
     if (aligned && (nb == 1 || nb == 2 || nb == 4 || nb == 8 || nb == 16)) rpw = nb >= 8 ? 1 : 8 / nb;
-    if (!rpw) return launch_generic<QT, IH, OH>(W, 0, rows, cols, x, T, y, rows, stream);
+    if (!rpw) return launch_generic<QT, IH, OH, AM>(W, 0, rows, cols, x, T, y, rows, stream, am);
     const long long nsteps = rows / rpw;
     const int rows_main = (int)(nsteps * rpw);
+    ArgmaxArgs am_fast = am;
+    if (rows_main < rows) am_fast.finalize = 0;  // the generic tail launch finalises
     if (nsteps > 0) {
         int st = BREAD_OK;
         const bool one = T == 1;
-#define BREAD_FAST(NB_)                                                                                \
-    case NB_:                                                                                          \
-        st = one ? launch_fast<QT, NB_, true, IH, OH>(W, nsteps, x, T, y, rows, stream)                \
-                 : launch_fast<QT, NB_, false, IH, OH>(W, nsteps, x, T, y, rows, stream);             \
+#define BREAD_FAST(NB_)                                                                                         \
+    case NB_:                                                                                                   \
+        st = AM    ? launch_fast<QT, NB_, true, IH, OH, AM>(W, nsteps, x, T, y, rows, stream, am_fast)          \
+             : one ? launch_fast<QT, NB_, true, IH, OH>(W, nsteps, x, T, y, rows, stream)                       \
+                   : launch_fast<QT, NB_, false, IH, OH>(W, nsteps, x, T, y, rows, stream);                    \
         break;
         switch (nb) {
             BREAD_FAST(1)
@@ -337,7 +404,7 @@ static int gemv_dispatch_q(const uint8_t *W, int rows, int cols, const void *x, 
 #undef BREAD_FAST
         if (st != BREAD_OK) return st;
     }
-    return launch_generic<QT, IH, OH>(W, rows_main, rows - rows_main, cols, x, T, y, rows, stream);
+    return launch_generic<QT, IH, OH, AM>(W, rows_main, rows - rows_main, cols, x, T, y, rows, stream, am);
 }
 
 // y[T x rows] = x[T x cols] * W^T for T <= GEMV_TMAX.
@@ -396,6 +463,34 @@ extern "C" int bread_matvec_batch_f32(const void *w, const float *x, float *y, i
                                          stream));
     }
     return BREAD_OK;
+}
+
+extern "C" int bread_lm_head_argmax(const void *w, const float *x, int rows, int cols, int qtype, int round_half,
+                                    float *logits, int *token, float *value, void *state, cudaStream_t stream)
+{
+    if (!w || !x || !token || !state) return set_error(BREAD_ERR_ARG, "lm_head_argmax: NULL pointer");
+    if (qtype != BREAD_QTYPE_Q4_K && qtype != BREAD_QTYPE_Q6_K && qtype != BREAD_QTYPE_Q8_0)
+        return set_error(BREAD_ERR_QTYPE, "lm_head_argmax: unknown qtype %d", qtype);
+    if (rows <= 0 || cols <= 0 || cols % block_elems(qtype))
+        return set_error(BREAD_ERR_ARG, "lm_head_argmax: rows=%d cols=%d", rows, cols);
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(state)) & 7)
+        return set_error(BREAD_ERR_ALIGN, "lm_head_argmax: x and state must be 8-byte aligned");
+    ArgmaxArgs am;
+    am.key = static_cast<unsigned long long *>(state);
+    am.ticket = reinterpret_cast<unsigned *>(am.key + 1);
+    am.token = token;
+    am.value = value;
+    am.round_half = round_half ? 1 : 0;
+    am.finalize = 1;
+    const uint8_t *W = static_cast<const uint8_t *>(w);
+    switch (qtype) {
+    case BREAD_QTYPE_Q4_K:
+        return gemv_dispatch_q<BREAD_QTYPE_Q4_K, false, false, true>(W, rows, cols, x, 1, logits, stream, am);
+    case BREAD_QTYPE_Q6_K:
+        return gemv_dispatch_q<BREAD_QTYPE_Q6_K, false, false, true>(W, rows, cols, x, 1, logits, stream, am);
+    default:
+        return launch_generic<BREAD_QTYPE_Q8_0, false, false, true>(W, 0, rows, cols, x, 1, logits, rows, stream, am);
+    }
 }
 
 extern "C" int bread_dequant(const void *w, float *out, long long n_blocks, int qtype, cudaStream_t stream)

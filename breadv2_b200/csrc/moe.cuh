@@ -190,9 +190,11 @@ struct StepArgs {
     unsigned long long *ll_pres, *ll_lg, *ll_a, *ll_as, *ll_h;
     size_t ll_pres_n, ll_lg_n, ll_a_n, ll_as_n, ll_h_n;  // words per parity
     size_t ll_reset;            // host only: bytes from ctrl zeroed before a one-block launch
-    // optional outputs (written by CTA 0)
+    // optional outputs (written by CTA 0): the routing of the launch's layer
+    // [T x K], or of every layer [L][T x K] when out_per_layer is set
     int *idx_out;
     float *w_out, *sg_out;
+    int out_per_layer;
     int *stats;                 // [L][2]: expert groups, pairs computed here
     unsigned long long *stamps; // [L][grid][STAMPS] %globaltimer at phase points of every CTA, or NULL
     // expert parallel

@@ -334,7 +334,7 @@ __device__ __forceinline__ ChunkInfo chunk_search(const RouteTabs &R, int c)
 // of squares sit in shared memory (ssq_l), computed by this CTA.
 template <int PER, bool LLM = false>
 __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *idx, float *w, float *rinv,
-                            float *sgw, bool outputs, unsigned long long *st, int *pick_i = nullptr,
+                            float *sgw, bool outputs, unsigned long long *st, int l, int *pick_i = nullptr,
                             float *pick_w = nullptr, float *pick_sg = nullptr,
                             const unsigned long long *llg = nullptr, const float *ssq_l = nullptr, uint32_t tag = 0)
 {
@@ -413,17 +413,20 @@ __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *
         *pick_w = my_w;
         *pick_sg = Ld.w_sg ? 1.0f / (1.0f + expf(-(score * r))) : 0.5f;
     }
+    // caller's copies: [T x K] of the launch's layer, or [L][T x K] when
+    // every layer is recorded (out_per_layer)
+    const size_t ob = a.out_per_layer ? (size_t)l * a.T : 0;
     if (lane < K) {
         idx[t * K + lane] = my_i;
         w[t * K + lane] = my_w;
-        if (outputs && a.idx_out) a.idx_out[t * K + lane] = my_i;
-        if (outputs && a.w_out) a.w_out[t * K + lane] = my_w;
+        if (outputs && a.idx_out) a.idx_out[(ob + t) * K + lane] = my_i;
+        if (outputs && a.w_out) a.w_out[(ob + t) * K + lane] = my_w;
     }
     if (lane == 0) {
         const float sg = Ld.w_sg ? 1.0f / (1.0f + expf(-(score * r))) : 0.5f;
         rinv[t] = r;
         sgw[t] = sg;
-        if (outputs && a.sg_out) a.sg_out[t] = sg;
+        if (outputs && a.sg_out) a.sg_out[ob + t] = sg;
     }
 }
 
@@ -475,7 +478,7 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
         if (warp == 0) {
             int e;
             float w, sg;
-            route_token<PER, LLM>(a, Ld, 0, R.idx, R.w, R.rinv, R.sgw, cta0, (st && lane == 0) ? st : nullptr, &e,
+            route_token<PER, LLM>(a, Ld, 0, R.idx, R.w, R.rinv, R.sgw, cta0, (st && lane == 0) ? st : nullptr, l, &e,
                                   &w, &sg, llg, ssq_l, tag);
             const int hs = Ld.sh_gate ? 1 : 0;
             const bool loc = lane < K && e >= a.lo && e < a.hi;
@@ -521,7 +524,7 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
         return;
     } else {
         for (int t = warp; t < T; t += 8)
-            route_token<PER, LLM>(a, Ld, t, R.idx, R.w, R.rinv, R.sgw, cta0, (st && tid == 0) ? st : nullptr,
+            route_token<PER, LLM>(a, Ld, t, R.idx, R.w, R.rinv, R.sgw, cta0, (st && tid == 0) ? st : nullptr, l,
                                   nullptr, nullptr, nullptr, llg, ssq_l, tag);
     }
     named_sync(BAR_CONS, ST_CONS);
@@ -1303,9 +1306,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             // one warp of the grid per token, then every CTA reads the result
             for (int t = bx * 8 + warp; t < T; t += G * 8) {
                 if (E <= 256)
-                    route_token<8>(a, Ld, t, a.ridx, a.rw, a.rinv, a.rsgw, true, nullptr);
+                    route_token<8>(a, Ld, t, a.ridx, a.rw, a.rinv, a.rsgw, true, nullptr, l);
                 else
-                    route_token<MOE_EMAX / 32>(a, Ld, t, a.ridx, a.rw, a.rinv, a.rsgw, true, nullptr);
+                    route_token<MOE_EMAX / 32>(a, Ld, t, a.ridx, a.rw, a.rinv, a.rsgw, true, nullptr, l);
             }
             grid_barrier(a, bar++, tid);
         }

@@ -36,22 +36,32 @@ constexpr int NOALLOC_MAX_DEVICES = 64;
 static std::mutex g_scratch_mu;
 static void *g_scratch_addr[NOALLOC_MAX_DEVICES] = {};
 
-// Device address of g_moe_scratch on the current device, looked up once per
-// device (the first call on a device does it, so that call should come before
-// any stream capture).
-static int scratch_address(void **out)
+// Device address of g_moe_scratch on the current device.  The first call on
+// a device looks it up, so that call should come before any stream capture.
+// Every later call made outside capture looks it up again (no allocation,
+// cheap), so an address from before a cudaDeviceReset -- which reloads the
+// module and moves the array -- is never handed to a kernel; a call on a
+// capturing stream cannot make the lookup and takes the last address found.
+static int scratch_address(cudaStream_t stream, void **out)
 {
     int dev = 0;
     BREAD_CUDA(cudaGetDevice(&dev), "moe_ffn_noalloc: cudaGetDevice");
     if (dev < 0 || dev >= NOALLOC_MAX_DEVICES)
         return set_error(BREAD_ERR_STATE, "moe_ffn_noalloc: device %d beyond %d", dev, NOALLOC_MAX_DEVICES);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    BREAD_CUDA(cudaStreamIsCapturing(stream, &cap), "moe_ffn_noalloc: cudaStreamIsCapturing");
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
+    if (cap == cudaStreamCaptureStatusNone) {
         void *p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_moe_scratch);
         if (e != cudaSuccess) return cuda_status(e, "moe_ffn_noalloc: cudaGetSymbolAddress");
         if (!p) return set_error(BREAD_ERR_CUDA, "moe_ffn_noalloc: no device address for the scratch array");
         g_scratch_addr[dev] = p;
+    } else if (!g_scratch_addr[dev]) {
+        return set_error(BREAD_ERR_STATE,
+                         "moe_ffn_noalloc: first call on device %d is inside stream capture; make one call outside "
+                         "capture first",
+                         dev);
     }
     *out = g_scratch_addr[dev];
     return BREAD_OK;
@@ -75,7 +85,7 @@ extern "C" int bread_moe_ffn_noalloc(const void *const *gate_ptrs, const void *c
                          "holds %zu; use bread_moe_ffn with a workspace",
                          T, H, I, E, top_k, need, NOALLOC_SCRATCH_BYTES);
     void *scratch = nullptr;
-    BREAD_TRY(scratch_address(&scratch));
+    BREAD_TRY(scratch_address(stream, &scratch));
     return bread_moe_ffn(gate_ptrs, up_ptrs, down_ptrs, W_r, w_sg, sh_gate, sh_up, sh_down, x, out, T, H, I, E, top_k,
                          idx_out, w_out, sg_out, scratch, NOALLOC_SCRATCH_BYTES, stream);
 }

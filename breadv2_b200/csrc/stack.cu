@@ -56,6 +56,10 @@ struct bread_stack {
     bool peers_set = false;
     float *peer_mb[bread::EP_MAXW] = {};
     int *stats_dev = nullptr;                   // [n_layers][2]: groups, pairs of the last step
+    int *rec_idx = nullptr;                     // [n_layers][max_tokens][top_k]: routing of the last step
+    float *rec_w = nullptr;                     // [n_layers][max_tokens][top_k]
+    float *rec_sg = nullptr;                    // [n_layers][max_tokens]
+    int rec_T = 0;                              // tokens of the last step
     unsigned long long *stamps_dev = nullptr;   // [n_layers][ctas][STAMPS]: phase points of the last profiled step
     int ctas = 0;                               // grid of the step kernel (one CTA per SM)
 };
@@ -161,6 +165,11 @@ extern "C" int bread_stack_create(bread_stack_t **out, const bread_stack_config_
         st->h_dev = (float *)p;
         if (!rc) rc = stack_alloc(st, &p, (size_t)c.n_layers * 2 * sizeof(int), "stack: stats");
         st->stats_dev = (int *)p;
+        const size_t nrec = (size_t)c.n_layers * c.max_tokens;
+        if (!rc) rc = stack_alloc(st, &p, nrec * (2 * c.top_k + 1) * 4, "stack: routing record");
+        st->rec_idx = (int *)p;
+        st->rec_w = reinterpret_cast<float *>(st->rec_idx + nrec * c.top_k);
+        st->rec_sg = st->rec_w + nrec * c.top_k;
         st->ctas = sm_count();
         if (!rc) rc = stack_alloc(st, &p, (size_t)c.n_layers * st->ctas * STAMPS * sizeof(unsigned long long), "stack: stamps");
         st->stamps_dev = (unsigned long long *)p;
@@ -311,6 +320,12 @@ static int stack_launch(bread_stack_t *st, float *h, int T, cudaStream_t s, unsi
     a.y = h;
     a.stats = st->stats_dev;
     a.stamps = stamps;
+    // every layer's routing [L][T x K] (CTA 0 writes a few words per layer)
+    a.idx_out = st->rec_idx;
+    a.w_out = st->rec_w;
+    a.sg_out = st->rec_sg;
+    a.out_per_layer = 1;
+    st->rec_T = T;
     a.ep_world = c.world;
     a.ep_rank = c.rank;
     a.ep_tmax = c.max_tokens;
@@ -372,6 +387,19 @@ extern "C" int bread_stack_routing_stats(const bread_stack_t *st, int *groups, i
         groups[l] = v[2 * l];
         pairs[l] = v[2 * l + 1];
     }
+    return BREAD_OK;
+}
+
+extern "C" int bread_stack_routing(const bread_stack_t *st, int *idx, float *w, float *sg_weight, int *T_out)
+{
+    if (!st || !idx || !w || !sg_weight) return set_error(BREAD_ERR_ARG, "stack_routing: NULL argument");
+    const int T = st->rec_T, K = st->cfg.top_k, L = st->cfg.n_layers;
+    if (T_out) *T_out = T;
+    if (!T) return set_error(BREAD_ERR_STATE, "stack_routing: no step has run");
+    // the record is [L][T x K] packed for the last step's T
+    BREAD_CUDA(cudaMemcpy(idx, st->rec_idx, (size_t)L * T * K * 4, cudaMemcpyDeviceToHost), "stack: routing idx");
+    BREAD_CUDA(cudaMemcpy(w, st->rec_w, (size_t)L * T * K * 4, cudaMemcpyDeviceToHost), "stack: routing w");
+    BREAD_CUDA(cudaMemcpy(sg_weight, st->rec_sg, (size_t)L * T * 4, cudaMemcpyDeviceToHost), "stack: routing sg");
     return BREAD_OK;
 }
 

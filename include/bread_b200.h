@@ -87,6 +87,21 @@ int bread_matvec_f32(const void *w, const float *x, float *y, int rows, int cols
 int bread_matvec_batch_f32(const void *w, const float *x, float *y, int rows, int cols, int qtype, int T,
                            cudaStream_t stream);
 
+/* Output head + greedy sampling on the device: compute_logits (main.cu:297-319,
+ * bread_matvec of the [rows x cols] lm head) followed by greedy_sample
+ * (main.cu:324-337), which copies all `rows` fp16 logits to the host and
+ * scans them.  Here each warp of the GEMV folds its rows into a running
+ * argmax and the last warp to finish writes *token (largest logit; among
+ * equal values the lowest row, like the reference's strict `>` scan; NaN
+ * never wins; 0 when every logit is NaN) and *value (that logit, or NULL to
+ * skip).  round_half = 1 compares the fp16-rounded logits greedy_sample sees;
+ * 0 compares fp32.  logits: optional fp32 [rows] copy (NULL to skip).
+ * x: fp32 [cols].  state: 16 bytes of device memory, 8-byte aligned, zeroed by
+ * the caller once before the first call; every call leaves it zeroed again
+ * (calls sharing one state must not overlap on the GPU).  Enqueue-only. */
+int bread_lm_head_argmax(const void *w, const float *x, int rows, int cols, int qtype, int round_half, float *logits,
+                         int *token, float *value, void *state, cudaStream_t stream);
+
 /* Bit-exact dequantisation of n_blocks consecutive blocks to fp32
  * (Q4_K/Q6_K: 256 values per block, Q8_0: 32).  Arithmetic of
  * layer_ops.cu:44-105 (exact fp16 scale decode, each product rounded). */
@@ -146,11 +161,13 @@ int bread_moe_ffn(const void *const *gate_ptrs, const void *const *up_ptrs, cons
  * synchronise the device.  Same arguments and results as bread_moe_ffn minus
  * the workspace: the scratch is a fixed 256 KiB device array inside the
  * library (present on every GPU that loads it, until exit), enough for e.g.
- * T <= 8 at H = 2048, I = 512, E = 256, top_k = 8; larger shapes return
- * BREAD_ERR_WORKSPACE.  Allocates nothing.  The first call on each device looks
- * up the array's device address (cudaGetSymbolAddress), so make it before any
- * stream capture.  All calls on a device share the array: calls that overlap
- * on the GPU race and must be ordered by the caller. */
+ * T <= 16 at H = 2048, I = 512, E = 256, top_k = 8; larger shapes return
+ * BREAD_ERR_WORKSPACE.  Allocates nothing.  The first call on each device
+ * looks up the array's device address (cudaGetSymbolAddress, no allocation),
+ * so make that first call before any stream capture; later calls outside
+ * capture look it up again, so an address from before a cudaDeviceReset is
+ * never used.  All calls on a device share the array: calls that overlap on
+ * the GPU race and must be ordered by the caller. */
 int bread_moe_ffn_noalloc(const void *const *gate_ptrs, const void *const *up_ptrs, const void *const *down_ptrs,
                           const float *W_r, const void *w_sg, const void *sh_gate, const void *sh_up,
                           const void *sh_down, const float *x, float *out, int T, int H, int I, int E, int top_k,
@@ -228,6 +245,11 @@ int bread_stack_profile_step(bread_stack_t *st, float *h, int T, cudaStream_t st
  * 21 tables built, 22 down stages done, 23 down columns stored.  *ctas
  * receives the grid size.  Synchronous. */
 int bread_stack_profile_stamps(const bread_stack_t *st, unsigned long long *out, size_t n_words, int *ctas);
+/* Routing of every layer of the last step (the device-side route_layer,
+ * one_layer.cu:937-992, as the step kernel ran it): idx/w [n_layers x T x
+ * top_k], sg_weight [n_layers x T] host arrays sized for that step's T
+ * (returned in *T_out).  Synchronous. */
+int bread_stack_routing(const bread_stack_t *st, int *idx, float *w, float *sg_weight, int *T_out);
 /* Per layer of the last step: expert groups computed here (distinct routed
  * experts + the shared expert) and (token, expert) pairs.  Synchronous. */
 int bread_stack_routing_stats(const bread_stack_t *st, int *groups, int *pairs);

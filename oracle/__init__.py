@@ -29,7 +29,6 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libbread_ref.so")
-DEFAULT_REF_SRC = "/root/reference"
 
 Q8_0, Q4_K, Q6_K = 8, 12, 14
 BLOCK_BYTES = {Q4_K: 144, Q6_K: 210, Q8_0: 34}
@@ -40,13 +39,32 @@ _I = ctypes.c_int
 _F = ctypes.c_float
 
 
+def reference_source() -> str | None:
+    """Where the reference checkout is: $BREAD_REF_SRC, else the
+    ``reference_path`` recorded in the repository's BASELINE.json; None when
+    neither names an existing directory (e.g. on a GPU box, which only uses
+    the prebuilt _ref/ library)."""
+    cand = os.environ.get("BREAD_REF_SRC")
+    if not cand:
+        try:
+            import json
+
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                cand = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    return cand if cand and os.path.isdir(cand) else None
+
+
 def build(ref_src: str | None = None, verbose: bool = False) -> None:
     """Compile liboracle.so and, when the reference checkout exists, _ref/."""
-    ref_src = ref_src or os.environ.get("BREAD_REF_SRC", DEFAULT_REF_SRC)
+    ref_src = ref_src or reference_source()
     targets = ["oracle"]
-    if os.path.isdir(ref_src):
+    cmd = ["make", "-s", "-C", HERE]
+    if ref_src and os.path.isdir(ref_src):
         targets.append("ref")
-    cmd = ["make", "-s", "-C", HERE, f"REF={ref_src}"] + targets
+        cmd.append(f"REF={ref_src}")
+    cmd += targets
     out = subprocess.run(cmd, capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError(f"oracle build failed:\n{out.stdout}\n{out.stderr}")
@@ -81,8 +99,26 @@ def lib() -> ctypes.CDLL:
         L.orc_moe_f64.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P]
         L.orc_moe_f32.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P]
         L.orc_rmsnorm_f64.argtypes = [_P, _P, _I, ctypes.c_double]
+        L.orc_synth_blocks.argtypes = [_P, ctypes.c_longlong, _I, ctypes.c_uint64, ctypes.c_uint64]
+        L.orc_synth_normal.argtypes = [_P, ctypes.c_longlong, _F, ctypes.c_uint64, ctypes.c_uint64, _I]
         _lib = L
     return _lib
+
+
+def synth_blocks(n_blocks: int, qtype: int, seed: int, stream_id: int) -> np.ndarray:
+    """Seeded synthetic blocks, the same bytes as breadv2_b200.synth_blocks_host."""
+    out = np.empty(n_blocks * BLOCK_BYTES[qtype], np.uint8)
+    if lib().orc_synth_blocks(_p(out), n_blocks, qtype, seed, stream_id):
+        raise ValueError(f"synth_blocks: bad qtype {qtype}")
+    return out
+
+
+def synth_normal(n: int, stddev: float, seed: int, stream_id: int, half: bool = False) -> np.ndarray:
+    """Seeded N(0, stddev^2) values (fp32, or fp16 bits as uint16), the same as
+    breadv2_b200.synth_normal_host."""
+    out = np.empty(n, np.uint16 if half else np.float32)
+    lib().orc_synth_normal(_p(out), n, stddev, seed, stream_id, 1 if half else 0)
+    return out
 
 
 def ref_available() -> bool:

@@ -349,60 +349,123 @@ void orc_swiglu(const float *g, const float *u, float *out, int n)
     }
 }
 
-/* One expert (or the shared expert) in fp64 for token x (fp32[H]):
- * gate/up Q4_K [I x H], down Q6_K [H x I]; out[H] += w * down(silu(gate x) * (up x)).
- * Mirrors the per-expert body of the expert loop, one_layer.cu:1966-1981
- * (gate, up, silu*mul, down, scale_accum), with every sum in fp64. */
-static void orc_expert_f64(const uint8_t *gate, const uint8_t *up, const uint8_t *down, const float *x, int H, int I,
-                           double w, double *out, double *gb, double *ub)
+/* One expert (or the shared expert) in fp64 for the n tokens routed to it
+ * (their x rows gathered in xs [n x H]): gate/up Q4_K [I x H], down Q6_K
+ * [H x I]; contrib[j][H] = w[j] * down(silu(gate x_j) * (up x_j)).  Mirrors
+ * the per-expert body of the expert loop, one_layer.cu:1966-1981 (gate, up,
+ * silu*mul, down, scale_accum), with every sum in fp64 and each weight block
+ * decoded once for all n tokens (the per-token sums are unchanged by that). */
+static void orc_expert_group_f64(const uint8_t *gate, const uint8_t *up, const uint8_t *down, const float *xs, int n,
+                                 int H, int I, const double *w, double *const *contrib, double *gb, double *ub)
 {
-    orc_matvec_f64(gate, ORC_Q4_K, x, gb, I, H, 1);
-    orc_matvec_f64(up, ORC_Q4_K, x, ub, I, H, 1);
-    for (int i = 0; i < I; i++) {
+    orc_matvec_f64(gate, ORC_Q4_K, xs, gb, I, H, n);
+    orc_matvec_f64(up, ORC_Q4_K, xs, ub, I, H, n);
+    for (size_t i = 0; i < (size_t)n * I; i++) {
         const double g = gb[i];
         gb[i] = (g / (1.0 + exp(-g))) * ub[i];
     }
-    /* down projection with an fp64 activation: dequantised rows in fp32
-     * (exact), products and sums in fp64 */
     const int nb = I / ORC_QK;
     float blk[ORC_QK];
     for (int r = 0; r < H; r++) {
         const uint8_t *row = down + (size_t)r * nb * ORC_Q6K_BYTES;
-        double s = 0.0;
+        for (int j = 0; j < n; j++) ub[j] = 0.0;  /* per-token row sums */
         for (int b = 0; b < nb; b++) {
             orc_dequant_q6k_block(row + (size_t)b * ORC_Q6K_BYTES, blk, 0);
-            for (int i = 0; i < ORC_QK; i++) s += (double)blk[i] * gb[b * ORC_QK + i];
+            for (int j = 0; j < n; j++) {
+                const double *a = gb + (size_t)j * I + b * ORC_QK;
+                double acc = ub[j];
+                for (int i = 0; i < ORC_QK; i++) acc += (double)blk[i] * a[i];
+                ub[j] = acc;
+            }
         }
-        out[r] += w * s;
+        for (int j = 0; j < n; j++) contrib[j][r] = w[j] * ub[j];
     }
 }
 
 /* MoE FFN of T tokens in fp64, given the routing: for each token,
  * out[t] = sum_k wt[t,k] * expert_{idx[t,k]}(x_t) + sg_weight[t] * shared(x_t).
  * gate_ptrs/up_ptrs/down_ptrs index experts by id (host pointers).  shared_*
- * may be NULL (no shared expert).  out is fp64 [T x H], overwritten. */
+ * may be NULL (no shared expert).  out is fp64 [T x H], overwritten.
+ * Work is grouped by expert (each weight block decoded once per call) and
+ * spread over OpenMP threads; every token's contributions are then added in
+ * k order, shared expert last, exactly as a token-by-token loop would. */
 int orc_moe_f64(const uint8_t *const *gate_ptrs, const uint8_t *const *up_ptrs, const uint8_t *const *down_ptrs,
                 const uint8_t *sh_gate, const uint8_t *sh_up, const uint8_t *sh_down, const float *x,
                 const int *idx, const float *wt, const float *sg_weight, int T, int H, int I, int top_k, double *out)
 {
-    double *gb = (double *)malloc((size_t)I * sizeof(double));
-    double *ub = (double *)malloc((size_t)I * sizeof(double));
-    if (!gb || !ub) return -2;
-    for (int t = 0; t < T; t++) {
-        double *o = out + (size_t)t * H;
-        const float *xt = x + (size_t)t * H;
-        for (int r = 0; r < H; r++) o[r] = 0.0;
-        for (int k = 0; k < top_k; k++) {
-            const int e = idx[(size_t)t * top_k + k];
-            orc_expert_f64(gate_ptrs[e], up_ptrs[e], down_ptrs[e], xt, H, I, (double)wt[(size_t)t * top_k + k], o, gb,
-                           ub);
-        }
-        if (sh_gate && sh_up && sh_down)
-            orc_expert_f64(sh_gate, sh_up, sh_down, xt, H, I, (double)sg_weight[t], o, gb, ub);
+    const int KS = top_k + 1;  /* slot top_k: the shared expert */
+    const int has_sh = sh_gate && sh_up && sh_down;
+    double *contrib = (double *)calloc((size_t)T * KS * H, sizeof(double));
+    /* groups: distinct routed experts in order of first use, then the shared expert */
+    int *gexp = (int *)malloc((size_t)(T * top_k + 1) * sizeof(int));
+    int *pair_g = (int *)malloc((size_t)T * top_k * sizeof(int));
+    if (!contrib || !gexp || !pair_g) {
+        free(contrib);
+        free(gexp);
+        free(pair_g);
+        return -2;
     }
-    free(gb);
-    free(ub);
-    return 0;
+    int ng = 0;
+    for (int q = 0; q < T * top_k; q++) {
+        int g = 0;
+        while (g < ng && gexp[g] != idx[q]) g++;
+        if (g == ng) gexp[ng++] = idx[q];
+        pair_g[q] = g;
+    }
+    const int ngt = ng + (has_sh ? 1 : 0);
+    int fail = 0;
+#pragma omp parallel
+    {
+        float *xs = (float *)malloc((size_t)T * H * sizeof(float));
+        double *gb = (double *)malloc((size_t)T * I * sizeof(double));
+        double *ub = (double *)malloc((size_t)T * (I > H ? I : H) * sizeof(double));
+        double *w = (double *)malloc((size_t)T * sizeof(double));
+        double **dst = (double **)malloc((size_t)T * sizeof(double *));
+        if (!xs || !gb || !ub || !w || !dst) {
+#pragma omp atomic write
+            fail = 1;
+        } else {
+#pragma omp for schedule(dynamic, 1)
+            for (int g = 0; g < ngt; g++) {
+                int n = 0;
+                if (g < ng) {
+                    for (int q = 0; q < T * top_k; q++)
+                        if (pair_g[q] == g) {
+                            const int t = q / top_k, k = q % top_k;
+                            memcpy(xs + (size_t)n * H, x + (size_t)t * H, (size_t)H * sizeof(float));
+                            w[n] = (double)wt[q];
+                            dst[n] = contrib + ((size_t)t * KS + k) * H;
+                            n++;
+                        }
+                    const int e = gexp[g];
+                    orc_expert_group_f64(gate_ptrs[e], up_ptrs[e], down_ptrs[e], xs, n, H, I, w, dst, gb, ub);
+                } else {
+                    for (int t = 0; t < T; t++) {
+                        memcpy(xs + (size_t)t * H, x + (size_t)t * H, (size_t)H * sizeof(float));
+                        w[t] = (double)sg_weight[t];
+                        dst[t] = contrib + ((size_t)t * KS + top_k) * H;
+                    }
+                    orc_expert_group_f64(sh_gate, sh_up, sh_down, xs, T, H, I, w, dst, gb, ub);
+                }
+            }
+        }
+        free(xs);
+        free(gb);
+        free(ub);
+        free(w);
+        free(dst);
+    }
+    if (!fail)
+        for (int t = 0; t < T; t++)
+            for (int r = 0; r < H; r++) {
+                double o = 0.0;
+                for (int k = 0; k < KS; k++) o += contrib[((size_t)t * KS + k) * H + r];
+                out[(size_t)t * H + r] = o;
+            }
+    free(contrib);
+    free(gexp);
+    free(pair_g);
+    return fail ? -2 : 0;
 }
 
 /* The reference's fp32 expert block, structured as expert_bench.cu:158-179:
@@ -455,4 +518,102 @@ void orc_rmsnorm_f64(const double *x, double *y, int n, double eps)
     for (int i = 0; i < n; i++) ss += x[i] * x[i];
     const double inv = 1.0 / sqrt(ss / (double)n + eps);
     for (int i = 0; i < n; i++) y[i] = x[i] * inv;
+}
+
+/* ------------------------------------------------------------------ */
+/* Seeded synthetic inputs (benchmark data)                            */
+/* ------------------------------------------------------------------ */
+/* A host-only restatement of this repository's own counter-based generator
+ * (breadv2_b200/csrc/synth.cu; not reference code), so that the reference
+ * arm of bench.py builds its weights and activations without loading the
+ * product library.  Must give the same bytes: tests/test_oracle.py compares
+ * the two.  Values: a splitmix-style 64-bit mix of (seed, stream) keys and a
+ * counter; N(0,1) is a centred Irwin-Hall sum of the four 16-bit fields of
+ * one hash, scaled by sqrt(3)/65536 in one fp32 multiply. */
+static uint64_t orc_mix64(uint64_t z)
+{
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+static uint64_t orc_hash_key(uint64_t seed, uint64_t stream)
+{
+    return orc_mix64(seed ^ orc_mix64(stream + 0x632BE59BD9B4E019ull));
+}
+static uint64_t orc_hash3(uint64_t key, uint64_t ctr) { return orc_mix64(key + ctr); }
+static int orc_ih4(uint64_t h)
+{
+    return (int)(h & 0xFFFF) + (int)((h >> 16) & 0xFFFF) + (int)((h >> 32) & 0xFFFF) + (int)(h >> 48) - 131070;
+}
+static float orc_abs_normal(uint64_t h, float scale)
+{
+    int v = orc_ih4(h);
+    if (v < 0) v = -v;
+    return (float)v * scale;
+}
+
+static void orc_synth_block(uint8_t *dst, int qtype, uint64_t key, long long b)
+{
+    const uint64_t base = (uint64_t)b * 32u;
+    const float s3 = (float)(1e-3 * 1.7320508075688772 / 65536.0);
+    if (qtype == ORC_Q4_K) {
+        for (int i = 0; i < 18; ++i) {
+            const uint64_t h = orc_hash3(key, base + i);
+            for (int k = 0; k < 8; ++k) dst[8 * i + k] = (uint8_t)(h >> (8 * k));
+        }
+        const uint16_t d = orc_f2h(orc_abs_normal(orc_hash3(key, base + 20), s3));
+        const uint16_t m = orc_f2h(orc_abs_normal(orc_hash3(key, base + 21), s3));
+        dst[0] = (uint8_t)d;
+        dst[1] = (uint8_t)(d >> 8);
+        dst[2] = (uint8_t)m;
+        dst[3] = (uint8_t)(m >> 8);
+    } else if (qtype == ORC_Q6_K) {
+        for (int i = 0; i < 24; ++i) {
+            const uint64_t h = orc_hash3(key, base + i);
+            for (int k = 0; k < 8; ++k) dst[8 * i + k] = (uint8_t)(h >> (8 * k));
+        }
+        const uint64_t hs0 = orc_hash3(key, base + 24), hs1 = orc_hash3(key, base + 25);
+        for (int k = 0; k < 16; ++k) {
+            const uint8_t byte = (uint8_t)((k < 8 ? hs0 : hs1) >> (8 * (k & 7)));
+            dst[192 + k] = (uint8_t)(int8_t)((int)(byte & 63) - 32);
+        }
+        uint16_t d = orc_f2h(orc_abs_normal(orc_hash3(key, base + 26), s3));
+        if (orc_hash3(key, base + 27) & 1) d |= 0x8000u;
+        dst[208] = (uint8_t)d;
+        dst[209] = (uint8_t)(d >> 8);
+    } else {
+        for (int i = 0; i < 5; ++i) {
+            const uint64_t h = orc_hash3(key, base + i);
+            for (int k = 0; k < 8 && 8 * i + k < ORC_Q80_BYTES; ++k) dst[8 * i + k] = (uint8_t)(h >> (8 * k));
+        }
+        const uint16_t d = orc_f2h(orc_abs_normal(orc_hash3(key, base + 6), (float)(1e-2 * 1.7320508075688772 / 65536.0)));
+        dst[0] = (uint8_t)d;
+        dst[1] = (uint8_t)(d >> 8);
+    }
+}
+
+int orc_synth_blocks(uint8_t *dst, long long n_blocks, int qtype, uint64_t seed, uint64_t stream_id)
+{
+    const int bb = orc_block_bytes(qtype);
+    if (!bb || !dst || n_blocks < 0) return 1;
+    const uint64_t key = orc_hash_key(seed, stream_id);
+    for (long long b = 0; b < n_blocks; ++b) orc_synth_block(dst + b * bb, qtype, key, b);
+    return 0;
+}
+
+/* n values of N(0, stddev^2): fp32 (half_out = 0) or fp16 bits (half_out = 1). */
+int orc_synth_normal(void *dst, long long n, float stddev, uint64_t seed, uint64_t stream_id, int half_out)
+{
+    if (!dst || n < 0) return 1;
+    const uint64_t key = orc_hash_key(seed, stream_id);
+    const float inv = (float)(1.7320508075688772 / 65536.0);
+    for (long long i = 0; i < n; ++i) {
+        const float v = ((float)orc_ih4(orc_hash3(key, (uint64_t)i)) * inv) * stddev;
+        if (half_out)
+            ((uint16_t *)dst)[i] = orc_f2h(v);
+        else
+            ((float *)dst)[i] = v;
+    }
+    return 0;
 }

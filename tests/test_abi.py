@@ -103,3 +103,17 @@ def test_synth_host_deterministic_and_distributed():
     assert sc.min() == -32 and sc.max() == 31
     x = bb.synth_normal_host(1 << 16, 1.0, 1, 2)
     assert abs(x.mean()) < 0.02 and abs(x.std() - 1.0) < 0.02
+
+
+@pytest.mark.parametrize("qt", [12, 14, 8])
+def test_oracle_synth_equals_library_synth(orc, qt):
+    """The oracle's host restatement of the seeded generator (used by the
+    bench's CPU legs so that they load no product code) gives the library's
+    bytes."""
+    import breadv2_b200 as bb
+
+    assert np.array_equal(orc.synth_blocks(3001, qt, 7, 3), bb.synth_blocks_host(3001, qt, 7, 3))
+    a = orc.synth_normal(10007, 0.02, 5, 6)
+    assert np.array_equal(a.view(np.uint32), bb.synth_normal_host(10007, 0.02, 5, 6).view(np.uint32))
+    assert np.array_equal(orc.synth_normal(4099, 0.02, 5, 6, half=True),
+                          bb.synth_normal_host(4099, 0.02, 5, 6, half=True))

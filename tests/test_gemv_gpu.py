@@ -140,3 +140,94 @@ def test_lm_head_q6k_full_size(cuda, orc):
     wr = w.view(rows, rb)[torch.from_numpy(pick).to(cuda)].cpu().numpy().reshape(-1)
     ref = orc.matvec_f64(wr, 14, x1, 512, cols)
     assert orc.rel_l2(y1.cpu().numpy()[pick], ref) < TOL
+
+
+# ---- f1: lm head + greedy sample on the device ------------------------------
+def _expected_token(orc, ref64, gpu_logits, round_half):
+    """The oracle's greedy token (fp64 logits), accepting any row whose logit is
+    within fp32-summation noise of the top (then the GPU's own order decides)."""
+    top = float(ref64.max())
+    tol = 1e-4 * max(1.0, abs(top)) + (abs(top) * 2.0 ** -10 if round_half else 0.0)
+    return set(np.nonzero(ref64 >= top - tol)[0].tolist())
+
+
+@pytest.mark.parametrize("qt,rows,cols", [(14, 8192, 2048), (12, 4097, 512), (12, 3000, 2048), (8, 1000, 1024)])
+@pytest.mark.parametrize("round_half", [1, 0])
+def test_lm_head_argmax(cuda, orc, qt, rows, cols, round_half):
+    """bread_lm_head_argmax against the oracle's logits and against its own
+    logits output (which must be bit-equal to bread_matvec_f32's).  4097 rows
+    of Q4_K with cols=512 run a fast launch plus a generic tail launch; Q8_0 the
+    generic kernel only.  Two calls in a row share the state."""
+    rng = np.random.default_rng(rows + qt)
+    w = B.matrix(qt, rng, rows, cols)
+    wd = dev(w, cuda)
+    state = torch.zeros(2, dtype=torch.int64, device=cuda)
+    for call in range(2):
+        x = rng.standard_normal(cols).astype(np.float32)
+        xd = dev(x, cuda)
+        logits = torch.empty(rows, device=cuda)
+        tok, val = bb.lm_head_argmax(wd, xd, rows, cols, qt, round_half=bool(round_half), state=state, logits=logits)
+        y = bb.matvec_f32(wd, xd, rows, cols, qt)
+        torch.cuda.synchronize()
+        assert torch.equal(logits, y), "fused logits differ from bread_matvec_f32"
+        yl = y.cpu().numpy()
+        cmp = yl.astype(np.float16).astype(np.float32) if round_half else yl
+        assert int(tok.item()) == int(np.argmax(cmp)), f"call {call}"  # np.argmax: first of the maxima
+        assert float(val.item()) == float(cmp.max())
+        assert int(tok.item()) in _expected_token(orc, orc.matvec_f64(w, qt, x, rows, cols), yl, round_half)
+        assert torch.all(state == 0), "state re-zeroed for the next call"
+
+
+def test_lm_head_argmax_ties_lowest_row(cuda):
+    """Identical top rows: the lowest index wins (greedy_sample's strict `>`)."""
+    rng = np.random.default_rng(5)
+    rows, cols = 2048, 2048
+    w = B.matrix(14, rng, rows, cols).reshape(rows, -1)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = bb.matvec_f32(dev(w.reshape(-1), cuda), dev(x, cuda), rows, cols, 14).cpu().numpy()
+    top = int(np.argmax(y))
+    for r in (1500, 777, 1999):
+        w[r] = w[top]
+    tok, _ = bb.lm_head_argmax(dev(w.reshape(-1), cuda), dev(x, cuda), rows, cols, 14, round_half=False)
+    torch.cuda.synchronize()
+    assert int(tok.item()) == min(top, 777)
+
+
+def test_lm_head_argmax_full_head(cuda, orc):
+    """Config 2's 248320 x 2048 Q6_K output head: the fused argmax equals the
+    first maximum of the GPU's own logits and is the oracle's top token up to
+    fp32 noise."""
+    rows, cols = 248320, 2048
+    w = bb.synth_blocks(rows * cols // 256, 14, 99, 1, device=cuda)
+    x = bb.synth_normal(cols, 1.0, 99, 2, device=cuda)
+    tok, val = bb.lm_head_argmax(w, x, rows, cols, 14, round_half=True)
+    y = bb.matvec_f32(w, x, rows, cols, 14)
+    torch.cuda.synchronize()
+    yh = y.half().float().cpu().numpy()
+    assert int(tok.item()) == int(np.argmax(yh)) and float(val.item()) == float(yh.max())
+    ref = orc.matvec_f64(w.cpu().numpy(), 14, x.cpu().numpy(), rows, cols)
+    assert int(tok.item()) in _expected_token(orc, ref, y.cpu().numpy(), True)
+
+
+# ---- f4: the attention / SSM projection GEMVs of one_layer_forward ----------
+# (rows, cols, qtype) as one_layer.cu calls bread_matvec with the model's
+# dimensions (bread.h:32-52): q_proj 8192 x 2048 and k/v_proj 512 x 2048
+# (:1527-1532), SSM qkv 8192 x 2048, z 4096 x 2048, alpha/beta 32 x 2048
+# (:1639-1646), o_proj and ssm_out 2048 x 4096 (:1763, :1784).
+PROJ = [(12, 8192, 2048), (12, 512, 2048), (14, 512, 2048), (12, 4096, 2048), (12, 32, 2048), (12, 2048, 4096)]
+
+
+@pytest.mark.parametrize("qt,rows,cols", PROJ)
+def test_projection_shapes(cuda, orc, qt, rows, cols):
+    rng = np.random.default_rng(rows ^ cols ^ qt)
+    w = B.matrix(qt, rng, rows, cols)
+    wd = dev(w, cuda)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = bb.matvec_f32(wd, dev(x, cuda), rows, cols, qt).cpu().numpy()
+    assert orc.rel_l2(y, orc.matvec_f64(w, qt, x, rows, cols)) < TOL
+    # the fp16 form the reference calls (d_normed half in, half out)
+    xh = x.astype(np.float16)
+    yh = torch.empty(rows, dtype=torch.float16, device=cuda)
+    bb.matvec(wd, dev(xh, cuda), yh, rows, cols, qt)
+    ref = orc.matvec_f64(w, qt, xh.astype(np.float32), rows, cols)
+    assert orc.rel_l2(yh.float().cpu().numpy(), ref) < TOL

@@ -35,13 +35,13 @@ def _layer(dev, H, I, E, seed):
     return tabs, W_r, w_sg, shared, (gate, up, down)
 
 
-def _noalloc(tabs, W_r, w_sg, shared, x, out, I, K, idx, w, sg):
+def _noalloc(tabs, W_r, w_sg, shared, x, out, I, K, idx, w, sg, stream=None):
     T, H = x.shape
     E = W_r.shape[0]
     p = bb._p
     return bb.lib().bread_moe_ffn_noalloc(p(tabs[0]), p(tabs[1]), p(tabs[2]), p(W_r), p(w_sg), p(shared[0]),
                                           p(shared[1]), p(shared[2]), p(x), p(out), T, H, I, E, K, p(idx), p(w),
-                                          p(sg), bb._s(None))
+                                          p(sg), bb._s(stream))
 
 
 @pytest.mark.parametrize("T", [1, 8, 16])
@@ -65,9 +65,35 @@ def test_noalloc_matches_workspace_entry(cuda, T):
     assert bb.device_error() == 0
 
 
-def test_noalloc_rejects_oversized_shapes(cuda):
-    """Shapes whose scratch exceeds the fixed array are refused before any GPU work."""
-    H, I, E, K, T = 2048, 512, 256, 8, 64
+def test_noalloc_t16_on_a_side_stream(cuda):
+    """The largest accepted shape at the config sizes (T = 16), two calls
+    ordered on a non-default stream, both equal to the workspace entry point."""
+    H, I, E, K, T = 2048, 512, 256, 8, 16
+    tabs, W_r, w_sg, shared, _keep = _layer(cuda, H, I, E, seed=23)
+    x = bb.synth_normal(T * H, 1.0, 23, 4100, device=cuda).view(T, H)
+    base = bb.synth_normal(T * H, 3.0, 23, 5100, device=cuda).view(T, H)
+    ref = base.clone()
+    bb.moe_ffn(*tabs, W_r, w_sg, shared, x, ref, I, K)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    outs = [base.clone(), base.clone()]
+    idx = torch.empty(T, K, dtype=torch.int32, device=cuda)
+    w = torch.empty(T, K, dtype=torch.float32, device=cuda)
+    sg = torch.empty(T, dtype=torch.float32, device=cuda)
+    side.wait_stream(torch.cuda.current_stream())
+    for out in outs:  # back to back on the side stream: ordered, so they do not race on the array
+        assert _noalloc(tabs, W_r, w_sg, shared, x, out, I, K, idx, w, sg, stream=side) == 0, bb.last_error()
+    side.synchronize()
+    for call, out in enumerate(outs):
+        assert _rel(out - base, ref - base) < TOL, f"call {call}"
+    assert bb.device_error() == 0
+
+
+@pytest.mark.parametrize("T", [17, 64])
+def test_noalloc_rejects_oversized_shapes(cuda, T):
+    """Shapes whose scratch exceeds the fixed array are refused before any GPU
+    work: at the config sizes T = 16 is the largest accepted, 17 is refused."""
+    H, I, E, K = 2048, 512, 256, 8
     dummy = torch.zeros(16, dtype=torch.int64, device=cuda)
     x = torch.zeros(T, H, device=cuda)
     st = bb.lib().bread_moe_ffn_noalloc(bb._p(dummy), bb._p(dummy), bb._p(dummy), bb._p(x), None, None, None, None,
