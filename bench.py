@@ -189,7 +189,9 @@ class CpuLayerSampler:
     def run_layer(self, layer, h, W, sg):
         """One layer for T tokens: returns seconds spent in the reference code."""
         np, o = self.np, self.oracle
-        x = (h / np.sqrt((h.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + 1e-6)).astype(np.float32)
+        # rmsnorm_inplace (one_layer.cu:158-180): x * rms * post_attention_norm.weight
+        nw = o.synth_normal(H, 0.1, self.seed, self._sid(layer, 8, 0)) + np.float32(1.0)
+        x = (h / np.sqrt((h.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + 1e-6) * nw).astype(np.float32)
         t0 = time.perf_counter()
         if self.kind == "reference":
             idx, wt, sgw = o.ref_route(x, W, sg, K_TOP)
@@ -262,8 +264,119 @@ def run_reference(args, rank: int, world: int) -> int:
                          "threads": threads, **host_info()},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    # the reference's own GPU kernels on this box, beside its CPU path (extra key)
+    try:
+        import torch
+
+        if torch.cuda.is_available() and oracle.refgpu_available():
+            line["reference_gpu"] = reference_gpu_bar()
+    except Exception as ex:
+        line["reference_gpu"] = {"error": f"{type(ex).__name__}: {ex}"[:300]}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def reference_gpu_bar() -> dict:
+    """The reference's OWN GPU path on this B200 (kernels.cu compiled for
+    sm_100a from its sources, oracle/_ref/libbread_refgpu.so): its
+    bread_matvec on configs 1 and 2 (a CUDA graph of back-to-back launches
+    over 256 distinct weight copies, > L2, as our arm measures them) and the
+    expert_bench.cu:182-194 serial launch loop for one MoE block at T = 1
+    (8 routed + 1 shared expert: 5 launches each, fp16 activations), over 16
+    distinct expert sets.  Timed with CUDA events; a measurement beside the
+    CPU reference, not its value."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    import oracle
+
+    L = oracle.refgpu()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+
+    def sp():  # the current stream at call time (the capture stream inside a graph)
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    out = {"kernel": "kernels.cu dequant_q4k/q6k_matvec (one CTA per row, 256 threads), sm_100a build"}
+    peak = peaks()[0]
+
+    def graph_us(fn, n):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(3):
+                fn(i)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                fn(i)
+        g.replay()
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            t = e0.elapsed_time(e1) * 1e3 / n
+            best = t if best is None else min(best, t)
+        return best
+
+    ncopy = 256
+    for name, qt, rows, cols, blk in (("config1_q4k_512x2048", 12, 512, 2048, 144),
+                                      ("config2_q6k_2048x512", 14, 2048, 512, 210)):
+        nb = rows * cols // 256
+        wall = torch.from_numpy(oracle.synth_blocks(nb * ncopy, qt, 11, 20 + qt)).to(dev)
+        x = torch.from_numpy(oracle.synth_normal(cols, 1.0, 11, 30).astype(np.float16)).to(dev)
+        y = torch.empty(rows, dtype=torch.float16, device=dev)
+        mb = nb * blk
+        base = wall.data_ptr()
+
+        def f(i, base=base, mb=mb, x=x, y=y, rows=rows, cols=cols, qt=qt):
+            L.refgpu_matvec(ctypes.c_void_p(base + (i % ncopy) * mb), ctypes.c_void_p(x.data_ptr()),
+                            ctypes.c_void_p(y.data_ptr()), rows, cols, qt, sp())
+
+        us = graph_us(f, ncopy)
+        gbs = (mb + 2 * cols + 2 * rows) / (us * 1e-6) / 1e9
+        out[name] = {"us_per_launch": us, "GB_s": gbs, "frac": gbs / peak}
+        del wall
+    # one MoE block at T = 1: 9 experts (8 routed + shared) per call, 16 sets
+    Hh, Ii = H, I
+    nb_g, nb_d = Ii * Hh // 256, Hh * Ii // 256
+    nexp = 16 * 9
+    gate = torch.from_numpy(oracle.synth_blocks(nb_g * nexp, 12, 13, 1)).to(dev)
+    up = torch.from_numpy(oracle.synth_blocks(nb_g * nexp, 12, 13, 2)).to(dev)
+    down = torch.from_numpy(oracle.synth_blocks(nb_d * nexp, 14, 13, 3)).to(dev)
+    x = torch.from_numpy(oracle.synth_normal(Hh, 1.0, 13, 4).astype(np.float16)).to(dev)
+    hid = torch.empty(Hh, dtype=torch.float16, device=dev)
+    eg = torch.empty(Ii, dtype=torch.float16, device=dev)
+    eu = torch.empty(Ii, dtype=torch.float16, device=dev)
+    eo = torch.empty(Hh, dtype=torch.float16, device=dev)
+    wts = (ctypes.c_float * 9)(*([0.125] * 8 + [0.5]))
+    sets = []
+    for j in range(16):
+        e = [9 * j + k for k in range(9)]
+        sets.append(tuple((ctypes.c_void_p * 9)(*[t.data_ptr() + i * b for i in e])
+                          for t, b in ((gate, nb_g * 144), (up, nb_g * 144), (down, nb_d * 210))))
+
+    def blk(i):
+        g_, u_, d_ = sets[i % 16]
+        L.refgpu_expert_loop(g_, u_, d_, wts, 9, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(hid.data_ptr()),
+                             ctypes.c_void_p(eg.data_ptr()), ctypes.c_void_p(eu.data_ptr()),
+                             ctypes.c_void_p(eo.data_ptr()), Hh, Ii, sp())
+
+    us = graph_us(blk, 32)
+    nbytes = 9 * EXPERT_B
+    out["config3_expert_loop_t1"] = {"us_per_block": us, "launches_per_block": 1 + 9 * 5,
+                                     "GB_s": nbytes / (us * 1e-6) / 1e9, "frac": nbytes / (us * 1e-6) / 1e9 / peak,
+                                     "note": "experts only (the reference routes on the host, one_layer.cu:937-992)"}
+    del gate, up, down
+    torch.cuda.empty_cache()
+    return out
 
 
 def config_block(args, world):
@@ -299,6 +412,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
                         shared_expert=True, norm_eps=1e-6, seed=args.seed, rank=rank, world=world)
     if world > 1:
         st.connect_peers(dist)
+    parity = ep_parity(dist, rank, world, dev, args.seed) if world > 1 else None
     stream = torch.cuda.current_stream()
     inputs = [bb.synth_normal(T * H, 1.0, args.seed, 900 + i, device=dev).view(T, H) for i in range(N_INPUTS)]
     h = torch.empty(T, H, dtype=torch.float32, device=dev)
@@ -433,10 +547,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
             traffic = None
     timeline = layer_timeline(stamps)
 
-    matvec = None
+    matvec = configs = None
     if world == 1:
         st.close()  # free the stack before the GEMV weights
         matvec = matvec_bench(dev, hbm_peak)
+        try:
+            configs = configs_bench(dev, hbm_peak)
+        except Exception as ex:  # a side measurement: never lose the headline line to it
+            configs = {"error": f"{type(ex).__name__}: {ex}"[:300]}
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -464,12 +582,158 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
         "clocks": clk,
         "batch2": batch2,
         "matvec": matvec,
+        "configs_1_4": configs,
+        "ep_parity": parity,
     }
     print(json.dumps(line), flush=True)
     st.close()
     if dist is not None:
         dist.destroy_process_group()
     return 0
+
+
+def graph_time_us(fn, n_iter: int, reps: int = 3) -> float:
+    """Device time per call of `fn(i)` (i = 0..n_iter-1), captured into one CUDA
+    graph and replayed (launch gaps of a Python loop would dominate kernels of
+    a few microseconds): best of `reps` replays, CUDA events on the stream."""
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(n_iter):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) * 1e3 / n_iter
+        best = t if best is None else min(best, t)
+    del g
+    return best
+
+
+def configs_bench(dev, hbm_peak) -> dict:
+    """BASELINE configs 1-4 on one GPU (each a separate measurement beside the
+    config-5 headline):
+      1  Q4_K 512 x 2048 expert gate GEMV,  2  Q6_K 2048 x 512 expert down GEMV:
+         a CUDA graph of back-to-back bread_matvec_f32 launches over 256 distinct
+         weight copies (151 / 220 MB, > L2); bytes = weights + x + y;
+      3  one MoE block at T = 1 (router + 8 routed + shared expert) and
+      4  the same block for k in {1, 2, 4, 8, 16} tokens (speculative verify):
+         bread_moe_ffn over one resident layer of 256 + 1 experts, 16 distinct
+         seeded inputs cycled (~144 distinct experts, > L2); bytes = distinct
+         experts touched x 2,039,808 + the fp32 router + activations."""
+    import numpy as np
+    import torch
+
+    import breadv2_b200 as bb
+
+    out = {}
+    ncopy = 256
+    for name, qt, rows, cols, blk in (("config1_q4k_512x2048", 12, 512, 2048, 144),
+                                      ("config2_q6k_2048x512", 14, 2048, 512, 210)):
+        nb = rows * cols // 256
+        wall = bb.synth_blocks(nb * ncopy, qt, 11, 20 + qt, device=dev)
+        x = bb.synth_normal(cols, 1.0, 11, 30, device=dev)
+        y = torch.empty(rows, device=dev)
+        mb = nb * blk
+
+        def f(i, wall=wall, x=x, y=y, mb=mb, rows=rows, cols=cols, qt=qt):
+            bb.matvec_f32(wall[(i % ncopy) * mb:(i % ncopy + 1) * mb], x, rows, cols, qt, y=y)
+
+        us = graph_time_us(f, ncopy)
+        gbs = (mb + 4 * cols + 4 * rows) / (us * 1e-6) / 1e9
+        out[name] = {"shape": [rows, cols], "us_per_launch": us, "GB_s": gbs, "frac": gbs / hbm_peak,
+                     "launches": ncopy, "note": "CUDA graph of back-to-back launches, distinct weights each"}
+        del wall
+    torch.cuda.empty_cache()
+
+    # one resident MoE layer: 256 routed experts + shared, router, shared gate
+    Hh, Ii, Ee, Kk = H, I, E, K_TOP
+    nb_g, nb_d = Ii * Hh // 256, Hh * Ii // 256
+    gate = bb.synth_blocks(nb_g * Ee, 12, 12, 1, device=dev)
+    up = bb.synth_blocks(nb_g * Ee, 12, 12, 2, device=dev)
+    down = bb.synth_blocks(nb_d * Ee, 14, 12, 3, device=dev)
+    gb_, db_ = nb_g * 144, nb_d * 210
+    tabs = [bb.pointer_table([t.data_ptr() + e * b for e in range(Ee)], dev) for t, b in ((gate, gb_), (up, gb_),
+                                                                                             (down, db_))]
+    shared = (bb.synth_blocks(nb_g, 12, 12, 4, device=dev), bb.synth_blocks(nb_g, 12, 12, 5, device=dev),
+              bb.synth_blocks(nb_d, 14, 12, 6, device=dev))
+    W_r = bb.synth_normal(Ee * Hh, 0.02, 12, 7, device=dev).view(Ee, Hh)
+    w_sg = bb.synth_normal(Hh, 0.02, 12, 8, half=True, device=dev)
+    sweep = {}
+    for k in (1, 2, 4, 8, 16):
+        xs = [bb.synth_normal(k * Hh, 1.0, 12, 100 + 17 * k + i, device=dev).view(k, Hh) for i in range(16)]
+        outb = torch.zeros(k, Hh, device=dev)
+        ws = bb.alloc_workspace(k, Hh, Ii, Ee, Kk, device=dev)
+        distinct = []
+        for i in range(16):
+            idx, _, _ = bb.moe_ffn(*tabs, W_r, w_sg, shared, xs[i], outb, Ii, Kk, workspace=ws, want_routing=True)
+            distinct.append(len(set(idx.cpu().numpy().ravel().tolist())))
+
+        def f(i, xs=xs, outb=outb, ws=ws):
+            bb.moe_ffn(*tabs, W_r, w_sg, shared, xs[i % 16], outb, Ii, Kk, workspace=ws)
+
+        us = graph_time_us(f, 64)
+        groups = float(np.mean(distinct)) + 1
+        nbytes = groups * EXPERT_B + Ee * Hh * 4 + Hh * 2 + 2 * k * Hh * 4
+        sweep[str(k)] = {"tokens": k, "us_per_block": us, "tok_s_per_layer": k / (us * 1e-6),
+                         "experts_touched": groups, "GB_s": nbytes / (us * 1e-6) / 1e9,
+                         "frac": nbytes / (us * 1e-6) / 1e9 / hbm_peak}
+    out["config3_moe_block_t1"] = sweep["1"]
+    out["config4_verify_sweep"] = sweep
+    del gate, up, down
+    torch.cuda.empty_cache()
+    return out
+
+
+def ep_parity(dist, rank: int, world: int, dev, seed: int) -> dict:
+    """Expert-parallel correctness on the box that runs the scaling bench: a
+    3-layer stack at the full config shape split over the N ranks, one step at
+    T = 1 and one at T = 24, against a one-GPU stack from the same seed (rank
+    0).  Every rank must hold the same bits (all-gather)."""
+    import torch
+
+    import breadv2_b200 as bb
+    import oracle
+
+    res = {}
+    st = bb.ExpertStack(n_layers=3, max_tokens=24, seed=seed, rank=rank, world=world)
+    st.connect_peers(dist)
+    one = bb.ExpertStack(n_layers=3, max_tokens=24, seed=seed) if rank == 0 else None
+    for T in (1, 24):
+        h0 = bb.synth_normal(T * H, 1.0, seed, 4242 + T, device=dev).view(T, H)
+        h = h0.clone()
+        st.step(h)
+        torch.cuda.synchronize()
+        allh = [torch.empty_like(h) for _ in range(world)]
+        dist.all_gather(allh, h)
+        if rank == 0:
+            h1 = h0.clone()
+            one.step(h1)
+            torch.cuda.synchronize()
+            res[f"T{T}"] = {"rel_l2_vs_one_gpu": oracle.rel_l2(h.cpu().numpy(), h1.cpu().numpy()),
+                            "ranks_bitwise_equal": all(torch.equal(a, allh[0]) for a in allh)}
+    assert bb.device_error() == 0, "device-side wait timed out"
+    dist.barrier()
+    st.close()
+    if one is not None:
+        one.close()
+    if rank == 0:
+        res["layers"], res["config"] = 3, "H=2048 I=512 E=256 top-8 + shared, experts split over the ranks"
+    return res
 
 
 def matvec_bench(dev, hbm_peak) -> dict:

@@ -163,20 +163,93 @@ def moe_ffn(gate_tab, up_tab, down_tab, W_r, w_sg, shared, x, out, I: int, top_k
     return (idx, w, sg) if want_routing else None
 
 
+# ---- GGUF model files -----------------------------------------------------------
+class Gguf:
+    """Tensor index of a GGUF v2/v3 file (bread_gguf_*; gguf.c:306-411)."""
+
+    def __init__(self, path: str):
+        h = ctypes.c_void_p(0)
+        check(lib().bread_gguf_open(path.encode(), ctypes.byref(h)), "bread_gguf_open")
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            lib().bread_gguf_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def info(self) -> dict:
+        v, a = ctypes.c_uint32(0), ctypes.c_uint32(0)
+        n, off = ctypes.c_uint64(0), ctypes.c_uint64(0)
+        check(lib().bread_gguf_info(self.handle, ctypes.byref(v), ctypes.byref(n), ctypes.byref(a), ctypes.byref(off)),
+              "bread_gguf_info")
+        return {"version": v.value, "n_tensors": n.value, "alignment": a.value, "data_offset": off.value}
+
+    @staticmethod
+    def _dict(t) -> dict:
+        return {"name": t.name.decode(), "type": t.type, "dims": list(t.dims[: t.n_dims]), "offset": t.offset,
+                "size": t.size, "n_elems": t.n_elems}
+
+    def tensor(self, index: int) -> dict:
+        from ._lib import GgufTensor
+
+        t = GgufTensor()
+        check(lib().bread_gguf_tensor(self.handle, index, ctypes.byref(t)), "bread_gguf_tensor")
+        return self._dict(t)
+
+    def find(self, name: str):
+        """Tensor info by exact name, or None when absent."""
+        from ._lib import GgufTensor
+
+        t = GgufTensor()
+        if lib().bread_gguf_find(self.handle, name.encode(), ctypes.byref(t)) != 0:
+            return None
+        return self._dict(t)
+
+    def read(self, offset: int, nbytes: int):
+        import numpy as np
+
+        out = np.empty(nbytes, dtype=np.uint8)
+        check(lib().bread_gguf_read(self.handle, offset, out.ctypes.data_as(ctypes.c_void_p), nbytes), "bread_gguf_read")
+        return out
+
+
 # ---- expert stack ------------------------------------------------------------
 class ExpertStack:
     """All layers' experts resident on this GPU (or this rank's share of them),
     synthetic weights from a seed; ``step`` runs one decode step."""
 
     def __init__(self, n_layers=40, hidden=2048, inter=512, n_experts=256, top_k=8, max_tokens=64,
-                 shared_expert=True, norm_eps=1e-6, seed=1234, rank=0, world=1):
+                 shared_expert=True, norm_eps=1e-6, seed=1234, rank=0, world=1, norm_weight=True):
         self.cfg = StackConfig(n_layers, hidden, inter, n_experts, top_k, max_tokens, int(shared_expert), norm_eps,
-                               seed, rank, world)
+                               seed, rank, world, int(norm_weight))
         h = ctypes.c_void_p(0)
         self.handle = None
         self._opened = []
         check(lib().bread_stack_create(ctypes.byref(h), ctypes.byref(self.cfg)), "bread_stack_create")
         self.handle = h
+
+    @classmethod
+    def from_gguf(cls, path: str, n_layers: int, top_k: int = 8, max_tokens: int = 64, norm_eps: float = 1e-6,
+                  rank: int = 0, world: int = 1):
+        """The stack of a GGUF model file's first n_layers MoE layers
+        (bread_stack_create_gguf): shapes, shared expert and norm weights
+        come from the file."""
+        self = cls.__new__(cls)
+        self.cfg = StackConfig(n_layers, 0, 0, 0, top_k, max_tokens, 0, norm_eps, 0, rank, world, 0)
+        self.handle = None
+        self._opened = []
+        h = ctypes.c_void_p(0)
+        check(lib().bread_stack_create_gguf(ctypes.byref(h), path.encode(), ctypes.byref(self.cfg)),
+              "bread_stack_create_gguf")
+        self.handle = h
+        check(lib().bread_stack_get_config(h, ctypes.byref(self.cfg)), "bread_stack_get_config")
+        return self
 
     def close(self):
         if self.handle:
@@ -235,6 +308,17 @@ class ExpertStack:
         d = {k: (p.value or 0) for k, p in zip(keys, ptrs)}
         d["lo"], d["hi"] = lo.value, hi.value
         return d
+
+    def norm_weight(self, l: int):
+        """Layer l's pre-MoE RMSNorm weight (host fp32 [hidden]), or None for
+        unit weight."""
+        import numpy as np
+
+        out = np.zeros(self.cfg.hidden, dtype=np.float32)
+        has = ctypes.c_int(0)
+        check(lib().bread_stack_norm_weight(self.handle, l, out.ctypes.data_as(ctypes.c_void_p), ctypes.byref(has)),
+              "bread_stack_norm_weight")
+        return out if has.value else None
 
     def step(self, h, stream=None) -> None:
         """h: [T, hidden] fp32 on this device, updated in place."""

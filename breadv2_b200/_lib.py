@@ -36,12 +36,23 @@ SIGNATURES = {
     "bread_moe_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "bread_moe_ffn": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
     "bread_moe_ffn_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "bread_gguf_open": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "bread_gguf_close": (_I, [_P]),
+    "bread_gguf_info": (_I, [_P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(_U64), ctypes.POINTER(ctypes.c_uint32),
+                             ctypes.POINTER(_U64)]),
+    "bread_gguf_tensor": (_I, [_P, _U64, _P]),
+    "bread_gguf_find": (_I, [_P, ctypes.c_char_p, _P]),
+    "bread_gguf_read": (_I, [_P, _U64, _P, _U64]),
     "bread_stack_create": (_I, [ctypes.POINTER(_P), _P]),
+    "bread_stack_create_gguf": (_I, [ctypes.POINTER(_P), ctypes.c_char_p, _P]),
     "bread_stack_destroy": (_I, [_P]),
     "bread_stack_device_bytes": (_SZ, [_P]),
+    "bread_stack_get_config": (_I, [_P, _P]),
     "bread_stack_layer": (_I, [_P, _I] + [ctypes.POINTER(_P)] * 8 + [ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "bread_stack_norm_weight": (_I, [_P, _I, _P, ctypes.POINTER(_I)]),
     "bread_stack_mailbox": (_I, [_P, ctypes.POINTER(_P), ctypes.POINTER(_SZ)]),
     "bread_stack_set_peers": (_I, [_P, ctypes.POINTER(_P), _I]),
+    "bread_stack_set_peer_timeout": (_I, [_P, ctypes.c_double]),
     "bread_ipc_get_handle": (_I, [_P, _P]),
     "bread_ipc_open_handle": (_I, [_P, ctypes.POINTER(_P)]),
     "bread_ipc_close_handle": (_I, [_P]),
@@ -76,10 +87,15 @@ class BreadError(RuntimeError):
         super().__init__(f"{what}: {status_string(status)} ({last_error()})")
 
 
+class GgufTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_uint32), ("n_dims", ctypes.c_uint32),
+                ("dims", _U64 * 4), ("offset", _U64), ("size", _U64), ("n_elems", _U64)]
+
+
 class StackConfig(ctypes.Structure):
     _fields_ = [("n_layers", _I), ("hidden", _I), ("inter", _I), ("n_experts", _I), ("top_k", _I),
                 ("max_tokens", _I), ("shared_expert", _I), ("norm_eps", _F), ("seed", _U64), ("rank", _I),
-                ("world", _I)]
+                ("world", _I), ("norm_weight", _I)]
 
 
 _lib = None

@@ -25,7 +25,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-rdc=true", "-Xcompiler", "-fPIC", "-Xcompiler", "-O2",
          "--expt-relaxed-constexpr", f"-I{INCLUDE}", "-Wno-deprecated-gpu-targets"]
 
-SOURCES = ["errors.cu", "gemv.cu", "glue.cu", "moe.cu", "moe_h1.cu", "moe_h2.cu", "moe_h4.cu", "moe_h8.cu",
+SOURCES = ["errors.cu", "gemv.cu", "gguf.cu", "glue.cu", "moe.cu", "moe_h1.cu", "moe_h2.cu", "moe_h4.cu", "moe_h8.cu",
            "moe_h16.cu", "noalloc.cu", "stack.cu", "synth.cu"]
 HEADERS = ["common.cuh", "ptx.cuh", "qdot.cuh", "moe.cuh", "moe_kernel.cuh"]
 

@@ -125,6 +125,7 @@ static int moe_prepare(StepArgs &a, const float *x, const float *W_r, const void
     a.x = x;
     a.ep_world = 1;
     a.ep_tmax = T;
+    a.ep_wait_ns = EP_WAIT_NS;
     step_bind_workspace(a, workspace, L);
     a.ll_reset = L.ll_end;
     return BREAD_OK;

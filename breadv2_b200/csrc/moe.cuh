@@ -15,6 +15,7 @@ constexpr int MOE_TC = 8;        // (token, expert) pairs per chunk
 constexpr int MOE_ROWTILE = 32;  // gate/up rows per work item (one activation group)
 constexpr int MOE_RT3 = 16;      // down rows (= output columns of h) per tile
 constexpr int EP_MAXW = 8;       // expert-parallel ranks
+constexpr unsigned long long EP_WAIT_NS = 20000000000ull;  // default bound of a wait on another rank: 20 s
 
 __host__ __device__ constexpr size_t al16(size_t v) { return (v + 15) / 16 * 16; }
 
@@ -46,6 +47,8 @@ struct StepLayer {
     const uint8_t *sh_gate, *sh_up, *sh_down;        // shared expert, or NULL
     const float *W_r;                                // [E x H] fp32 router
     const __half *w_sg;                              // [H] fp16 shared-gate vector, or NULL
+    const float *norm_w;                             // [H] fp32 weight of the layer's pre-MoE RMSNorm
+                                                     // (post_attention_norm.weight), or NULL for 1
 };
 static_assert(sizeof(StepLayer) % 8 == 0, "layer descriptors are copied to shared memory in 8-byte words");
 
@@ -140,6 +143,7 @@ struct StepSmem {
     uint32_t rbuf, part, xsl, gring, abuf, dring, acc, bars, total;
     uint32_t xloc, xf, ssql;  // flagged-exchange mode: quantised tokens, layer input / intermediate, group sums
     uint32_t ldesc;           // copies of the L layer descriptors (StepArgs::layers)
+    uint32_t nwb;             // the layer's RMSNorm weight [H] (copied with the router rows)
     uint32_t r_idx, r_w, r_rinv, r_sgw, r_cnt, r_run, r_off, r_gexp, r_goff, r_gcnt, r_gcpre, r_ptok, r_pw, r_scal, r_ptr, r_chunk;
     uint32_t xslot, dslot;
     int NS_G, NS_D, RR, WPR;
@@ -147,16 +151,23 @@ struct StepSmem {
 
 // Expert-parallel mailbox of one rank: [3 slots][world][Tmax x H] fp32
 // partials written by every rank over NVLink, then one u64 arrival counter
-// per slot (monotonic; targets derive from the launch epoch).
+// per slot (monotonic; targets derive from the launch epoch) -- the
+// grid-barrier instantiations' exchange -- and, for decode launches of at
+// most LL_TMAX tokens, [3 slots][world][llT x H] flagged words {partial,
+// layer tag} that every rank stores into every rank's mailbox and polls in
+// its own (llT = min(Tmax, LL_TMAX)).
 constexpr int MB_SLOTS = 3;
 struct StepMailbox {
-    size_t ctr_off, total;
+    size_t ctr_off, ll_off, total;
+    int llT;
     __host__ __device__ static StepMailbox make(int world, int Tmax, int H)
     {
         StepMailbox m;
         const size_t data = (size_t)MB_SLOTS * world * Tmax * H * 4;
         m.ctr_off = (data + 255) / 256 * 256;
-        m.total = m.ctr_off + 256;
+        m.ll_off = m.ctr_off + 256;
+        m.llT = Tmax < LL_TMAX ? Tmax : LL_TMAX;
+        m.total = m.ll_off + (size_t)MB_SLOTS * world * m.llT * H * 8;
         return m;
     }
     __host__ __device__ static size_t data_off(int slot, int src, int world, int Tmax, int H)
@@ -200,6 +211,7 @@ struct StepArgs {
     // expert parallel
     float *ep_mb[EP_MAXW];
     int ep_world, ep_rank, ep_tmax;
+    unsigned long long ep_wait_ns;  // bound of every wait on another rank (then DEVERR_TIMEOUT)
     StepSmem sm;
 };
 

@@ -54,7 +54,6 @@ constexpr int BAR_CONS = 1;      // named barrier of the consumer warps
 constexpr int BAR_ALL = 2;       // consumers + producer: routing tables ready
 constexpr size_t SMEM_LIMIT = 232448;  // dynamic shared memory per CTA (227 KB)
 constexpr unsigned long long GRID_WAIT_NS = 2000000000ull;  // 2 s
-constexpr unsigned long long EP_WAIT_NS = 20000000000ull;   // 20 s (peers may start late)
 constexpr int ROUTE_DIST_T = 16;  // above this many tokens the grid routes them (one warp each)
 constexpr int ROUTER_TILE_T = 8;  // above this many tokens the router works in 16-row x 8-token units
 
@@ -103,15 +102,21 @@ static __device__ bool wait_counter(const unsigned long long *p, unsigned long l
 }
 
 // Bounded mbarrier wait that also gives up once the device error word is set.
-__device__ __forceinline__ void swait(uint64_t *bar, unsigned parity)
+// The spin loop is out of line: the waits are many and mostly succeed at
+// once, and the persistent kernel's instruction footprint is on its critical
+// path (every phase of every layer re-fetches its code).
+static __device__ __noinline__ void swait_slow(uint64_t *bar, unsigned parity)
 {
-    if (mbar_try_wait(bar, parity)) return;
     for (long long i = 0; i < SPIN_LIMIT; ++i) {
         if (mbar_try_wait(bar, parity)) return;
         if ((i & 1023) == 1023 && dev_failed()) return;
         if (i > 64) __nanosleep(32);
     }
     flag_error(DEVERR_TIMEOUT);
+}
+__device__ __forceinline__ void swait(uint64_t *bar, unsigned parity)
+{
+    if (!mbar_try_wait(bar, parity)) swait_slow(bar, parity);
 }
 
 // Flagged word *p once its tag equals `tag`: bounded poll (the grid-barrier
@@ -145,37 +150,71 @@ __device__ __forceinline__ uint32_t flagged_take(unsigned long long v, const uns
 // The words addr(k), k < N with bit k of `valid` set, polled as one batch --
 // every word still carrying an old tag is loaded again in the same round --
 // until all tags equal `tag` (bounded like flagged_wait).  r[k]: the words.
-template <int N, class Addr>
-__device__ __forceinline__ void flagged_poll(unsigned long long (&r)[N], unsigned valid, const Addr &addr, uint32_t tag)
+template <int N, class Addr, bool SYS = false>
+__device__ __forceinline__ void flagged_poll(unsigned long long (&r)[N], unsigned valid, const Addr &addr, uint32_t tag,
+                                             unsigned long long limit_ns = GRID_WAIT_NS)
 {
 #pragma unroll
-    for (int k = 0; k < N; ++k) r[k] = ((valid >> k) & 1u) ? ld_flagged(addr(k)) : 0ull;
-    unsigned pend = 0;
-#pragma unroll
-    for (int k = 0; k < N; ++k)
-        if (((valid >> k) & 1u) && (uint32_t)(r[k] >> 32) != tag) pend |= 1u << k;
+    for (int k = 0; k < N; ++k) r[k] = 0ull;
+    unsigned pend = valid;
     unsigned long long t0 = 0;
-    for (unsigned it = 0; pend; ++it) {
-        if (it > 2) __nanosleep(40);
+    // one copy of the loads: the first round loads every valid word, later
+    // rounds only those still carrying an old tag
+    for (unsigned it = 0;; ++it) {
 #pragma unroll
         for (int k = 0; k < N; ++k)
-            if ((pend >> k) & 1u) r[k] = ld_flagged(addr(k));
+            if ((pend >> k) & 1u) r[k] = SYS ? ld_flagged_sys(addr(k)) : ld_flagged(addr(k));
         unsigned np = 0;
 #pragma unroll
         for (int k = 0; k < N; ++k)
             if (((pend >> k) & 1u) && (uint32_t)(r[k] >> 32) != tag) np |= 1u << k;
         pend = np;
-        if (pend && (it & 31) == 31) {
+        if (!pend) return;
+        if (it > 2) __nanosleep(40);
+        if ((it & 31) == 31) {
             if (dev_failed()) return;
             const unsigned long long now = globaltimer();
             if (!t0) {
                 t0 = now;
-            } else if (now - t0 > GRID_WAIT_NS) {
+            } else if (now - t0 > limit_ns) {
                 flag_error(DEVERR_TIMEOUT);
                 return;
             }
         }
     }
+}
+
+// Sums V values per lane over groups of LPR consecutive lanes (LPR a power
+// of two, V a power of two <= LPR) with a transposed butterfly: each halving
+// step trades half of the lane's values with its partner, so V values take
+// V - 1 + log2(LPR / V) + ... shuffles instead of V * log2(LPR).  Returns the
+// fully reduced value of index q(lane) = the top log2(V) bits of
+// (lane % LPR) (lane bit log2(LPR)-1 is the most significant); every lane of
+// the group whose top bits equal q holds it.
+template <int V, int LPR>
+__device__ __forceinline__ float tr_reduce(float (&v)[V])
+{
+    const int lane = threadIdx.x & 31;
+    int n = V;
+#pragma unroll
+    for (int off = LPR / 2; off >= 1; off >>= 1) {
+        if (n > 1) {
+            const bool hi = (lane & off) != 0;
+            const int h = n / 2;
+#pragma unroll
+            for (int i = 0; i < V / 2; ++i) {
+                if (i < h) {
+                    const float keep = hi ? v[h + i] : v[i];
+                    const float give = hi ? v[i] : v[h + i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, give, off);
+                }
+            }
+            n = h;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+        }
+    }
+    return v[0];
 }
 
 // Grid-wide barrier number `idx` of this launch (all 256 consumer threads).
@@ -223,6 +262,16 @@ __device__ __forceinline__ unsigned long long *ep_counter(const StepArgs &a, int
 {
     const StepMailbox M = StepMailbox::make(a.ep_world, a.ep_tmax, a.H);
     return reinterpret_cast<unsigned long long *>(reinterpret_cast<uint8_t *>(a.ep_mb[rank]) + M.ctr_off) + slot;
+}
+
+// Decode mode, expert parallel: the flagged word of element oi (t * H + col)
+// of source rank `src`'s partial for mailbox slot `slot` in rank `dst`'s
+// mailbox.
+__device__ __forceinline__ unsigned long long *ep_ll_word(const StepArgs &a, int dst, int slot, int src, size_t oi)
+{
+    const StepMailbox M = StepMailbox::make(a.ep_world, a.ep_tmax, a.H);
+    unsigned long long *w = reinterpret_cast<unsigned long long *>(reinterpret_cast<uint8_t *>(a.ep_mb[dst]) + M.ll_off);
+    return w + ((size_t)slot * a.ep_world + src) * (size_t)M.llT * a.H + oi;
 }
 
 __device__ __forceinline__ const uint8_t *expert_ptr(const uint8_t *const *tab, const uint8_t *sh, int e, int E)
@@ -743,12 +792,19 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
 // at grid barriers (every CTA quantises the layer input itself).  Each
 // instantiation carries only its own paths, which keeps the decode
 // instruction footprint small.
-constexpr int MODE_LL = 0, MODE_SMALL = 1, MODE_BIG = 2;
+// MODE_LLEP: the decode mode with expert parallelism -- every rank runs the
+// flagged-word decode step on its own experts, and each column tile's owner
+// stores its partial sums as flagged words into every rank's mailbox over
+// NVLink, then polls the N partials of its tile in its own mailbox and adds
+// them in rank order (so every rank holds the same bits and routes the same):
+// no arrival counters, no system-scope release, no grid barrier.
+constexpr int MODE_LL = 0, MODE_SMALL = 1, MODE_BIG = 2, MODE_LLEP = 3;
 template <int NBH, int NBI, int MODE>
 __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_constant__ StepArgs a)
 {
     constexpr bool BIG = MODE == MODE_BIG;
-    constexpr bool LL = MODE == MODE_LL;
+    constexpr bool LL = MODE == MODE_LL || MODE == MODE_LLEP;
+    constexpr bool LLEP = MODE == MODE_LLEP;
     using C = SCfg<NBH, NBI>;
     using GH = typename C::GH;
     using GI = typename C::GI;
@@ -866,6 +922,9 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 const int r = bx + rl * G;
                 bytes += r < E ? H * 4 : (r == E && Ld.w_sg ? H * 2 : 0);
             }
+            // the RMSNorm weight travels with the rows (needed first in phase A)
+            const bool nwc = Ld.norm_w && a.norm_eps >= 0.0f && !(reinterpret_cast<uintptr_t>(Ld.norm_w) & 15);
+            if (nwc) bytes += H * 4;
             if (lane == 0) {
                 if (bytes)
                     mbar_arrive_expect_tx(rbar, bytes);
@@ -880,6 +939,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 else if (r == E && Ld.w_sg)
                     bulk_g2s(rbuf + (size_t)lane * H, Ld.w_sg, H * 2, rbar);
             }
+            if (nwc && lane == 31) bulk_g2s(smem + m.nwb, Ld.norm_w, H * 4, rbar);
         };
         // One gate/up sub-stage (SR gate rows + SR up rows from row r0) at ring
         // cursor g (called by the issuing lane).
@@ -1038,7 +1098,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         const float *pmb = nullptr;  // layer l-1's partials in this rank's mailbox (EP)
         if (ep && l > 0) {
             const int s = ep_slot(a.L, l - 1);
-            if (tid == 0) wait_counter(ep_counter(a, a.ep_rank, s), ep_target(a, l - 1, epoch, NT), true, EP_WAIT_NS);
+            if (tid == 0) wait_counter(ep_counter(a, a.ep_rank, s), ep_target(a, l - 1, epoch, NT), true, a.ep_wait_ns);
             named_sync(BAR_CONS, ST_CONS);
             src = in_of(a, l - 1);
             pmb = a.ep_mb[a.ep_rank] + mb_slot_off(s, a);
@@ -1064,6 +1124,35 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     v.z += q.z;
                     v.w += q.w;
                 }
+            return v;
+        };
+        // the layer input times the RMSNorm weight (rmsnorm_inplace,
+        // one_layer.cu:158-180: x * rms * w; the rms factor is applied later
+        // to the logits and to the activations' group scales)
+        // (one-GPU and small-batch modes: the copy in shared memory, landed
+        // with the router rows -- so that wait comes first; a misaligned
+        // weight vector is read from global memory)
+        const float *nw = norm ? Ld.norm_w : nullptr;
+        if (!BIG && nw) {
+            swait(rbar, (unsigned)(l & 1));
+            if (!(reinterpret_cast<uintptr_t>(Ld.norm_w) & 15)) nw = reinterpret_cast<const float *>(smem + m.nwb);
+        }
+        // (decode mode: xf already holds the weighted input, see below)
+        auto xinw = [&](size_t i) -> float {
+            if constexpr (LL) return xin(i);
+            const float v = xin(i);
+            return nw ? v * nw[i & (size_t)(H - 1)] : v;  // H: a power of two
+        };
+        auto xin4w = [&](size_t i) -> float4 {  // i: a multiple of 4
+            if constexpr (LL) return xin4(i);
+            float4 v = xin4(i);
+            if (nw) {
+                const float4 w = *reinterpret_cast<const float4 *>(nw + (i & (size_t)(H - 1)));
+                v.x *= w.x;
+                v.y *= w.y;
+                v.z *= w.z;
+                v.w *= w.w;
+            }
             return v;
         };
         if constexpr (LL) {
@@ -1101,6 +1190,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     const int gi = g0 + 8 * k;
                     const float x = gi < ngr ? xf[gi * 32 + lane] : 0.0f;
                     v[k] = x * x;
+                    // RMSNorm weight: the lane rewrites the value it read
+                    if (nw && gi < ngr) xf[gi * 32 + lane] = x * nw[(gi * 32 + lane) & (H - 1)];
                 }
 #pragma unroll
                 for (int o = 16; o; o >>= 1)
@@ -1111,6 +1202,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     for (int k = 0; k < 4; ++k)
                         if (g0 + 8 * k < ngr) ssql[g0 + 8 * k] = v[k];
             }
+            if (nw) named_sync(BAR_CONS, ST_CONS);  // the weighted input, read by every warp below
         } else {
             // (1) this CTA's share of the int16 quantisation (+ group sums of squares)
             const int ngr = T * (H / 32);
@@ -1118,7 +1210,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 const float v = xin((size_t)gi * 32 + lane);
                 const float ss = warp_sum(v * v);
                 if (lane == 0) a.ssq[gi] = ss;
-                const int q = quant32(v, a.xs + gi, lane);
+                const int q = quant32(nw ? v * nw[((size_t)gi * 32 + lane) & (size_t)(H - 1)] : v, a.xs + gi,
+                                      lane);
                 const int e = gi * 32 + lane, t = e / H;  // H: a power of two
                 a.xq[(size_t)t * H + xq_pos(e - t * H)] = (int16_t)q;
             }
@@ -1149,7 +1242,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 const int tn = T - t0 < 8 ? T - t0 : 8;
                 for (int i = tid; i < tn * (H / 4); i += ST_CONS) {
                     const int t = i / (H / 4), c4 = i % (H / 4);
-                    reinterpret_cast<float4 *>(xst)[i] = xin4((size_t)(t0 + t) * H + 4 * c4);
+                    reinterpret_cast<float4 *>(xst)[i] = xin4w((size_t)(t0 + t) * H + 4 * c4);
                 }
                 named_sync(BAR_CONS, ST_CONS);
                 for (int rr = 0; rr < 2; ++rr) {
@@ -1224,8 +1317,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                             for (int j = 0; j < 4; ++j) {
                                 const int c = cb + 4 * lane + 128 * j;
                                 const bool in = c < c0 + seg;
-                                x0[j] = in ? xin4((size_t)t0 * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-                                x1[j] = (in && two) ? xin4((size_t)(t0 + 1) * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                                x0[j] = in ? xin4w((size_t)t0 * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                                x1[j] = (in && two) ? xin4w((size_t)(t0 + 1) * H + c) : make_float4(0.f, 0.f, 0.f, 0.f);
                             }
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
@@ -1257,7 +1350,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                         float s0 = 0.0f;
                         for (int c = c0 + lane; c < c0 + seg; c += 32) {
                             const float w = row < E ? wr[c] : __half2float(wh[c]);
-                            s0 = fmaf(w, xin((size_t)t * H + c), s0);
+                            s0 = fmaf(w, xinw((size_t)t * H + c), s0);
                         }
                         s0 = warp_sum(s0);
                         if (lane == 0) part[(rl * m.WPR + qt) * T + t] = s0;
@@ -1316,7 +1409,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             const unsigned long long *llg = LL ? a.ll_lg + par_of(l) * a.ll_lg_n : nullptr;
             const unsigned long long *pres =
                 (LL && E + (Ld.w_sg ? 1 : 0) < G) ? a.ll_pres + par_of(l) * a.ll_pres_n : nullptr;
-            if (E <= 256)
+            if (LL || E <= 256)  // (decode mode is used only with E <= 256)
                 route_tables<8, BIG, LL>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql, tg);
             else
                 route_tables<MOE_EMAX / 32, BIG, LL>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql, tg);
@@ -1357,38 +1450,39 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                         swait(gfull + g.slot, (unsigned)g.phase);
                     }
                     for (int j = 0; has_rows && j < ci.np; ++j) {
-                        if (ci.np > 1 || j == 0) {
+                        {
                             const int t = RT.ptok[ci.p0 + j];
                             const float rsc = norm ? RT.rinv[t] : 1.0f;
 #pragma unroll
                             for (int cp = 0; cp < GH::CP; ++cp)
                                 load_slice_q4k(X[cp], xq_of(j, t), xs_of(j, t), QK * (cp * 8 + bb) + 64 * sub, rsc);
                         }
-                        float gs[C::SPI], us[C::SPI];
+                        // v[2s] = gate row dot, v[2s+1] = up row dot of sub-stage s
+                        constexpr int NV = 2 * C::SPI;
+                        float v[NV];
 #pragma unroll
                         for (int s = 0; s < C::SPI; ++s) {
                             const uint8_t *grow =
                                 gring + (size_t)gR.ahead(s, NS_G).slot * C::STB + (size_t)rs * GH::ROWB;
                             const uint8_t *urow = grow + (size_t)C::SR * GH::ROWB;
-                            gs[s] = 0.0f;
-                            us[s] = 0.0f;
+                            v[2 * s] = 0.0f;
+                            v[2 * s + 1] = 0.0f;
 #pragma unroll
                             for (int cp = 0; cp < GH::CP; ++cp) {
-                                gs[s] += q4k_lane_dot(grow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
-                                us[s] += q4k_lane_dot(urow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                                v[2 * s] += q4k_lane_dot(grow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
+                                v[2 * s + 1] += q4k_lane_dot(urow + (size_t)(cp * 8 + bb) * Q4K_BYTES, sub, X[cp]);
                             }
                         }
-#pragma unroll
-                        for (int o = GH::LPR / 2; o; o >>= 1)
-#pragma unroll
-                            for (int s = 0; s < C::SPI; ++s) {
-                                gs[s] += __shfl_xor_sync(0xffffffffu, gs[s], o);
-                                us[s] += __shfl_xor_sync(0xffffffffu, us[s], o);
-                            }
-                        if (lr == 0)
-#pragma unroll
-                            for (int s = 0; s < C::SPI; ++s)
-                                abuf[j * MOE_ROWTILE + s * C::SR + rs] = gs[s] / (1.0f + expf(-gs[s])) * us[s];
+                        // transposed reduction over the row's lanes: lane group
+                        // q = top bits of lr holds value q (gate of sub-stage
+                        // q/2 when q is even); its up value sits LPR/NV lanes up
+                        static_assert(NV <= GH::LPR, "gate/up values per lane exceed the row's lanes");
+                        const float r = tr_reduce<NV, GH::LPR>(v);
+                        const float u = __shfl_xor_sync(0xffffffffu, r, GH::LPR / NV);
+                        if ((lr & (2 * GH::LPR / NV - 1)) == 0) {
+                            const int sidx = (lr / (GH::LPR / NV)) >> 1;
+                            abuf[j * MOE_ROWTILE + sidx * C::SR + rs] = r / (1.0f + expf(-r)) * u;
+                        }
                     }
                     __syncwarp();
                     if (lane == 0)
@@ -1565,14 +1659,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                                                                   sub & 1, L6, X[cp]);
                                     }
                                 }
-#pragma unroll
-                                for (int o = GI::LPR / 2; o; o >>= 1)
-#pragma unroll
-                                    for (int wi = 0; wi < DB; ++wi) v[wi] += __shfl_xor_sync(0xffffffffu, v[wi], o);
-                                if (lr == 0)
-#pragma unroll
-                                    for (int wi = 0; wi < DB; ++wi)
-                                        if (wb + wi < whi) my_acc[t * MOE_RT3 + (wb + wi) * GI::RPW + rho] += wgt * v[wi];
+                                // transposed reduction: lane group q of the
+                                // row's lanes holds step wb + q
+                                static_assert(DB <= GI::LPR, "down values per lane exceed the row's lanes");
+                                const float r = tr_reduce<DB, GI::LPR>(v);
+                                const int q = lr / (GI::LPR / DB);
+                                if ((lr & (GI::LPR / DB - 1)) == 0 && wb + q < whi)
+                                    my_acc[t * MOE_RT3 + (wb + q) * GI::RPW + rho] += wgt * r;
                             }
                         }
                         __syncwarp();
@@ -1648,6 +1741,28 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                         // this rank's partial -> slot [slot_l][ep_rank] of every rank's mailbox (NVLink stores)
                         const size_t off = mb_slot_off(slot_l, a) + (size_t)a.ep_rank * TH + oi;
                         for (int p = 0; p < a.ep_world; ++p) a.ep_mb[p][off] = s;
+                    } else if (LLEP) {
+                        // this rank's partial -> word [slot_l][ep_rank] of every
+                        // rank's mailbox (system-scope 64-bit stores over NVLink),
+                        // then every rank's partial of the element from this
+                        // rank's own mailbox, polled as one batch, added in rank
+                        // order after the residual
+                        for (int p = 0; p < a.ep_world; ++p)
+                            st_flagged_sys(ep_ll_word(a, p, slot_l, a.ep_rank, oi), __float_as_uint(s), tg);
+                        unsigned long long pw[EP_MAXW];
+                        const unsigned valid = (1u << a.ep_world) - 1u;
+                        auto pa = [&](int src) -> const unsigned long long * {
+                            return ep_ll_word(a, a.ep_rank, slot_l, src, oi);
+                        };
+                        flagged_poll<EP_MAXW, decltype(pa), true>(pw, valid, pa, tg, a.ep_wait_ns);
+                        float h = rv[k];
+#pragma unroll
+                        for (int src = 0; src < EP_MAXW; ++src)
+                            if (src < a.ep_world) h += __uint_as_float((uint32_t)pw[src]);
+                        if (l < a.L - 1)
+                            st_flagged(a.ll_h + par_of(l) * a.ll_h_n + oi, __float_as_uint(h), tg);
+                        else
+                            out[oi] = h;
                     } else if (LL && l < a.L - 1) {
                         st_flagged(a.ll_h + par_of(l) * a.ll_h_n + oi, __float_as_uint(rv[k] + s), tg);
                     } else {
@@ -1656,11 +1771,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 }
                 if (stamp) stamp_at(l, 23);
                 if (ep) {
-                    // system-scope releases by thread 0, after the CTA barrier
-                    // that orders every thread's partial stores before them
+                    // system-scope releases, one rank per thread (in parallel:
+                    // each release waits for the CTA's stores in flight), after
+                    // the CTA barrier that orders every thread's partial stores
+                    // before them (a release is cumulative over what its
+                    // thread has observed)
                     named_sync(BAR_CONS, ST_CONS);
-                    if (tid == 0)
-                        for (int p = 0; p < a.ep_world; ++p) red_release_sys(ep_counter(a, p, slot_l), 1ull);
+                    if (tid < a.ep_world) red_release_sys(ep_counter(a, tid, slot_l), 1ull);
                 }
                 named_sync(BAR_CONS, ST_CONS);
             }
@@ -1674,7 +1791,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
     // EP: the last layer's partials -> output columns owned by this CTA
     if (ep && !a.route_only) {
         const int s = ep_slot(a.L, a.L - 1);
-        if (tid == 0) wait_counter(ep_counter(a, a.ep_rank, s), ep_target(a, a.L - 1, epoch, NT), true, EP_WAIT_NS);
+        if (tid == 0) wait_counter(ep_counter(a, a.ep_rank, s), ep_target(a, a.L - 1, epoch, NT), true, a.ep_wait_ns);
         named_sync(BAR_CONS, ST_CONS);
         const float *src = in_of(a, a.L - 1);
         const float *pmb = a.ep_mb[a.ep_rank] + mb_slot_off(s, a);
@@ -1727,6 +1844,7 @@ static int step_layout(StepSmem &m, int T, int K, int E, int EL, int G, int mode
     const bool arena = mode == MODE_BIG;  // tiled router (no rows in smem), rings share one arena
     const bool ll = mode == MODE_LL;
     m.rbuf = take(arena ? 16 : (size_t)rr * C::H * 4, 128);
+    m.nwb = take(arena ? 16 : (size_t)C::H * 4, 128);
     m.part = take((size_t)8 * T * 4, 16);
     const int GM = (EL < T * K ? EL : T * K) + 1, PM = T * (K + 1);
     m.r_idx = take((size_t)T * K * 4, 16);
@@ -1815,10 +1933,11 @@ static int setup_nb()
     if (dev < 0 || dev >= MAX_DEVICES) return set_error(BREAD_ERR_STATE, "moe step: device %d", dev);
     std::lock_guard<std::mutex> lock(mu);
     if (!done[dev]) {
-        for (int mode = 0; mode < 3; ++mode) {
+        for (int mode = 0; mode < 4; ++mode) {
             auto kern = mode == MODE_LL      ? moe_step_kernel<NBH, NBI, MODE_LL>
                         : mode == MODE_SMALL ? moe_step_kernel<NBH, NBI, MODE_SMALL>
-                                             : moe_step_kernel<NBH, NBI, MODE_BIG>;
+                        : mode == MODE_BIG   ? moe_step_kernel<NBH, NBI, MODE_BIG>
+                                             : moe_step_kernel<NBH, NBI, MODE_LLEP>;
             BREAD_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LIMIT),
                        "moe step: shared-memory attribute");
             int n = 0;
@@ -1844,10 +1963,12 @@ static int launch_nb(StepArgs &a, cudaStream_t s)
     }();
     int mode = a.T > ROUTER_TILE_T ? MODE_BIG : MODE_SMALL;
     const int ndesc = a.layers ? a.L : 0;
-    if (mode == MODE_SMALL && !no_flagged && a.ll_pres && a.ep_world == 1 && !a.route_only && a.T <= LL_TMAX &&
-        G <= LL_GMAX && (a.L == 1 || a.ll_h) &&
+    // expert-parallel decode needs the inter-layer words and its mailbox words
+    const bool ll_ep_ok = a.ep_world == 1 || (a.ll_h && a.T <= StepMailbox::make(a.ep_world, a.ep_tmax, a.H).llT);
+    if (mode == MODE_SMALL && !no_flagged && a.ll_pres && ll_ep_ok && !a.route_only && a.T <= LL_TMAX &&
+        a.E <= 256 && G <= LL_GMAX && (a.L == 1 || a.ll_h) &&
         step_layout<NBH, NBI>(a.sm, a.T, a.top_k, a.E, a.hi - a.lo, G, MODE_LL, ndesc) == 0)
-        mode = MODE_LL;
+        mode = a.ep_world > 1 ? MODE_LLEP : MODE_LL;
     else if (step_layout<NBH, NBI>(a.sm, a.T, a.top_k, a.E, a.hi - a.lo, G, mode, ndesc))
         return set_error(BREAD_ERR_ARG, "moe step: T=%d H=%d I=%d does not fit in shared memory", a.T, a.H, a.I);
     cudaLaunchConfig_t cfg = {};
@@ -1864,6 +1985,8 @@ static int launch_nb(StepArgs &a, cudaStream_t s)
         BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_BIG>, a), "moe step launch");
     else if (mode == MODE_SMALL)
         BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_SMALL>, a), "moe step launch");
+    else if (mode == MODE_LLEP)
+        BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_LLEP>, a), "moe step launch");
     else
         BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_LL>, a), "moe step launch");
     return BREAD_OK;

@@ -136,6 +136,19 @@ __device__ __forceinline__ unsigned long long ld_flagged(const unsigned long lon
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
     return v;
 }
+// The same at system scope: words another GPU stores into this GPU's memory
+// (or this GPU into a peer's) over NVLink.
+__device__ __forceinline__ void st_flagged_sys(unsigned long long *p, uint32_t payload, uint32_t tag)
+{
+    const unsigned long long w = ((unsigned long long)tag << 32) | payload;
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_flagged_sys(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
+    return v;
+}
 __device__ __forceinline__ unsigned long long globaltimer()
 {
     unsigned long long t;

@@ -15,8 +15,10 @@
 // of every layer plus the shared expert of layers l with l % world == r; the
 // router (2 MB per layer) is replicated, so all ranks route identically and no
 // dispatch exchange is needed.
+#include <stdio.h>
 #include <string.h>
 
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -27,13 +29,14 @@ namespace bread {
 
 // stream ids of the synthetic tensors: (layer, kind, expert)
 static uint64_t sid(int layer, int kind, int e) { return ((uint64_t)layer << 32) | ((uint64_t)kind << 24) | (uint64_t)e; }
-enum { K_GATE = 0, K_UP = 1, K_DOWN = 2, K_SH_GATE = 3, K_SH_UP = 4, K_SH_DOWN = 5, K_ROUTER = 6, K_SGVEC = 7 };
+enum { K_GATE = 0, K_UP = 1, K_DOWN = 2, K_SH_GATE = 3, K_SH_UP = 4, K_SH_DOWN = 5, K_ROUTER = 6, K_SGVEC = 7, K_NORM = 8 };
 
 struct LayerW {
     uint8_t *gate, *up, *down;           // local experts, contiguous [n_local x ...]
     uint8_t *sh_gate, *sh_up, *sh_down;  // NULL when another rank owns the shared expert
     float *W_r;
     __half *w_sg;
+    float *norm_w;                       // pre-MoE RMSNorm weight [H], or NULL (unit weight)
     const uint8_t **tab;                 // device: gate[E], up[E], down[E] pointer tables
 };
 
@@ -62,6 +65,7 @@ struct bread_stack {
     int rec_T = 0;                              // tokens of the last step
     unsigned long long *stamps_dev = nullptr;   // [n_layers][ctas][STAMPS]: phase points of the last profiled step
     int ctas = 0;                               // grid of the step kernel (one CTA per SM)
+    unsigned long long ep_wait_ns = bread::EP_WAIT_NS;  // bound of each wait on another rank
 };
 
 using namespace bread;
@@ -83,11 +87,181 @@ extern "C" int bread_stack_destroy(bread_stack_t *st)
     return BREAD_OK;
 }
 
-extern "C" int bread_stack_create(bread_stack_t **out, const bread_stack_config_t *cfg)
+namespace bread {
+
+// Where a stack's weights come from: the seeded generator (bread_stack_create)
+// or a GGUF model file (bread_stack_create_gguf).  Every call fills device
+// memory on stream s.
+struct WeightSource {
+    virtual ~WeightSource() {}
+    // experts [lo, lo + n) of matrix kind (K_GATE / K_UP / K_DOWN) of layer l
+    virtual int experts(int l, int kind, int lo, int n, uint8_t *dst, size_t expert_bytes, cudaStream_t s) = 0;
+    virtual bool has_shared(int l) = 0;
+    virtual int shared(int l, int kind, uint8_t *dst, size_t bytes, cudaStream_t s) = 0;
+    virtual int router(int l, float *dst, size_t n, cudaStream_t s) = 0;
+    virtual bool has_shared_gate(int l) = 0;
+    virtual int shared_gate(int l, __half *dst, int H, cudaStream_t s) = 0;
+    virtual bool has_norm(int l) = 0;
+    virtual int norm(int l, float *dst, int H, cudaStream_t s) = 0;
+};
+
+struct SynthSource : WeightSource {
+    const bread_stack_config_t &c;
+    explicit SynthSource(const bread_stack_config_t &cfg) : c(cfg) {}
+    int experts(int l, int kind, int lo, int n, uint8_t *dst, size_t eb, cudaStream_t s) override
+    {
+        const int qt = kind == K_DOWN ? BREAD_QTYPE_Q6_K : BREAD_QTYPE_Q4_K;
+        const size_t bb = kind == K_DOWN ? Q6K_BYTES : Q4K_BYTES;
+        for (int j = 0; j < n; ++j)
+            BREAD_TRY(bread_synth_blocks(dst + j * eb, (long long)(eb / bb), qt, c.seed, sid(l, kind, lo + j), s));
+        return BREAD_OK;
+    }
+    bool has_shared(int) override { return c.shared_expert != 0; }
+    int shared(int l, int kind, uint8_t *dst, size_t bytes, cudaStream_t s) override
+    {
+        const int qt = kind == K_SH_DOWN ? BREAD_QTYPE_Q6_K : BREAD_QTYPE_Q4_K;
+        const size_t bb = kind == K_SH_DOWN ? Q6K_BYTES : Q4K_BYTES;
+        return bread_synth_blocks(dst, (long long)(bytes / bb), qt, c.seed, sid(l, kind, 0), s);
+    }
+    int router(int l, float *dst, size_t n, cudaStream_t s) override
+    {
+        return bread_synth_normal_f32(dst, (long long)n, 0.02f, c.seed, sid(l, K_ROUTER, 0), s);
+    }
+    bool has_shared_gate(int) override { return c.shared_expert != 0; }
+    int shared_gate(int l, __half *dst, int H, cudaStream_t s) override
+    {
+        return bread_synth_normal_f16(dst, H, 0.02f, c.seed, sid(l, K_SGVEC, 0), s);
+    }
+    bool has_norm(int) override { return c.norm_weight != 0; }
+    int norm(int l, float *dst, int H, cudaStream_t s) override
+    {
+        // post_attention_norm.weight stand-in: 1 + 0.1 * N(0,1), seeded
+        std::vector<float> w((size_t)H);
+        bread_synth_normal_f32_host(w.data(), H, 0.1f, c.seed, sid(l, K_NORM, 0));
+        for (float &v : w) v += 1.0f;
+        BREAD_CUDA(cudaMemcpyAsync(dst, w.data(), (size_t)H * 4, cudaMemcpyHostToDevice, s), "stack: upload norm weight");
+        BREAD_CUDA(cudaStreamSynchronize(s), "stack: upload norm weight");
+        return BREAD_OK;
+    }
+};
+
+// GGUF model file: byte ranges of the named tensors copied through a pinned
+// staging buffer (loader.c:156-206 names and expert byte ranges: expert k of
+// a *_exps tensor starts at k * size / n_experts).
+struct GgufSource : WeightSource {
+    bread_gguf_t *g = nullptr;
+    void *stage = nullptr;
+    static constexpr size_t STAGE = 32u << 20;
+    ~GgufSource() override
+    {
+        if (stage) cudaFreeHost(stage);
+        bread_gguf_close(g);
+    }
+    static std::string name(int l, const char *what)
+    {
+        char b[96];
+        snprintf(b, sizeof b, "blk.%d.%s.weight", l, what);
+        return b;
+    }
+    bool find(int l, const char *what, bread_gguf_tensor_t *t)
+    {
+        char saved[512];
+        snprintf(saved, sizeof saved, "%s", bread_last_error());
+        const bool ok = bread_gguf_find(g, name(l, what).c_str(), t) == BREAD_OK;
+        set_error(BREAD_OK, "%s", saved);  // absence of an optional tensor is not an error
+        return ok;
+    }
+    int need(int l, const char *what, uint32_t type, bread_gguf_tensor_t *t)
+    {
+        if (bread_gguf_find(g, name(l, what).c_str(), t) != BREAD_OK)
+            return set_error(BREAD_ERR_ARG, "stack_create_gguf: no tensor %s", name(l, what).c_str());
+        if (t->type != type)
+            return set_error(BREAD_ERR_QTYPE, "stack_create_gguf: %s has ggml type %u, expected %u", name(l, what).c_str(),
+                             t->type, type);
+        return BREAD_OK;
+    }
+    // bytes [off, off + n) of the data section -> device dst
+    int copy(uint64_t off, void *dst, size_t n, cudaStream_t s)
+    {
+        uint8_t *d = static_cast<uint8_t *>(dst);
+        for (size_t done = 0; done < n;) {
+            const size_t k = n - done < STAGE ? n - done : STAGE;
+            BREAD_CUDA(cudaStreamSynchronize(s), "stack: gguf staging");
+            BREAD_TRY(bread_gguf_read(g, off + done, stage, k));
+            BREAD_CUDA(cudaMemcpyAsync(d + done, stage, k, cudaMemcpyHostToDevice, s), "stack: gguf upload");
+            done += k;
+        }
+        BREAD_CUDA(cudaStreamSynchronize(s), "stack: gguf upload");
+        return BREAD_OK;
+    }
+    int experts(int l, int kind, int lo, int n, uint8_t *dst, size_t eb, cudaStream_t s) override
+    {
+        const char *what = kind == K_GATE ? "ffn_gate_exps" : kind == K_UP ? "ffn_up_exps" : "ffn_down_exps";
+        bread_gguf_tensor_t t;
+        BREAD_TRY(need(l, what, kind == K_DOWN ? BREAD_QTYPE_Q6_K : BREAD_QTYPE_Q4_K, &t));
+        const uint64_t ne = t.n_dims ? t.dims[t.n_dims - 1] : 0;
+        if (!ne || t.size / ne != eb || (uint64_t)lo + n > ne)
+            return set_error(BREAD_ERR_ARG, "stack_create_gguf: %s holds %llu experts of %llu bytes, need %zu-byte experts "
+                             "[%d, %d)", name(l, what).c_str(), (unsigned long long)ne,
+                             (unsigned long long)(ne ? t.size / ne : 0), eb, lo, lo + n);
+        return copy(t.offset + (uint64_t)lo * eb, dst, (size_t)n * eb, s);
+    }
+    bool has_shared(int l) override
+    {
+        bread_gguf_tensor_t t;
+        return find(l, "ffn_gate_shexp", &t);
+    }
+    int shared(int l, int kind, uint8_t *dst, size_t bytes, cudaStream_t s) override
+    {
+        const char *what = kind == K_SH_GATE ? "ffn_gate_shexp" : kind == K_SH_UP ? "ffn_up_shexp" : "ffn_down_shexp";
+        bread_gguf_tensor_t t;
+        BREAD_TRY(need(l, what, kind == K_SH_DOWN ? BREAD_QTYPE_Q6_K : BREAD_QTYPE_Q4_K, &t));
+        if (t.size != bytes)
+            return set_error(BREAD_ERR_ARG, "stack_create_gguf: %s is %llu bytes, expected %zu", name(l, what).c_str(),
+                             (unsigned long long)t.size, bytes);
+        return copy(t.offset, dst, bytes, s);
+    }
+    int router(int l, float *dst, size_t n, cudaStream_t s) override
+    {
+        bread_gguf_tensor_t t;
+        BREAD_TRY(need(l, "ffn_gate_inp", 0, &t));  // F32 (one_layer.cu:246-251)
+        if (t.size != n * 4) return set_error(BREAD_ERR_ARG, "stack_create_gguf: %s has the wrong size", name(l, "ffn_gate_inp").c_str());
+        return copy(t.offset, dst, n * 4, s);
+    }
+    bool has_shared_gate(int l) override
+    {
+        bread_gguf_tensor_t t;
+        return find(l, "ffn_gate_inp_shexp", &t);
+    }
+    int shared_gate(int l, __half *dst, int H, cudaStream_t s) override
+    {
+        bread_gguf_tensor_t t;
+        BREAD_TRY(need(l, "ffn_gate_inp_shexp", 1, &t));  // F16 (one_layer.cu:258-263)
+        if (t.size != (uint64_t)H * 2)
+            return set_error(BREAD_ERR_ARG, "stack_create_gguf: %s has the wrong size", name(l, "ffn_gate_inp_shexp").c_str());
+        return copy(t.offset, dst, (size_t)H * 2, s);
+    }
+    bool has_norm(int l) override
+    {
+        bread_gguf_tensor_t t;
+        return find(l, "post_attention_norm", &t);
+    }
+    int norm(int l, float *dst, int H, cudaStream_t s) override
+    {
+        bread_gguf_tensor_t t;
+        BREAD_TRY(need(l, "post_attention_norm", 0, &t));
+        if (t.size != (uint64_t)H * 4)
+            return set_error(BREAD_ERR_ARG, "stack_create_gguf: %s has the wrong size", name(l, "post_attention_norm").c_str());
+        return copy(t.offset, dst, (size_t)H * 4, s);
+    }
+};
+
+}  // namespace bread
+
+// Allocates every buffer of a stack and fills the weights from `src`.
+static int stack_build(bread_stack_t **out, const bread_stack_config_t &c, WeightSource &src)
 {
-    if (!out || !cfg) return set_error(BREAD_ERR_ARG, "stack_create: NULL argument");
     *out = nullptr;
-    const bread_stack_config_t c = *cfg;
     if (c.n_layers < 1) return set_error(BREAD_ERR_ARG, "stack_create: n_layers=%d", c.n_layers);
     BREAD_TRY(moe_check_shapes(c.max_tokens, c.hidden, c.inter, c.n_experts, c.top_k, true));
     if (c.world < 1 || c.world > EP_MAXW || c.rank < 0 || c.rank >= c.world || c.n_experts % c.world)
@@ -119,30 +293,32 @@ extern "C" int bread_stack_create(bread_stack_t **out, const bread_stack_config_
         L.up = (uint8_t *)p;
         if ((rc = stack_alloc(st, &p, down_b * st->n_local, "stack: down"))) break;
         L.down = (uint8_t *)p;
-        for (int j = 0; j < st->n_local && rc == BREAD_OK; ++j) {
-            const int e = st->lo + j;
-            rc = bread_synth_blocks(L.gate + j * gate_b, (long long)(gate_b / Q4K_BYTES), BREAD_QTYPE_Q4_K, c.seed, sid(l, K_GATE, e), s);
-            if (!rc) rc = bread_synth_blocks(L.up + j * gate_b, (long long)(gate_b / Q4K_BYTES), BREAD_QTYPE_Q4_K, c.seed, sid(l, K_UP, e), s);
-            if (!rc) rc = bread_synth_blocks(L.down + j * down_b, (long long)(down_b / Q6K_BYTES), BREAD_QTYPE_Q6_K, c.seed, sid(l, K_DOWN, e), s);
-        }
-        if (rc) break;
-        if (c.shared_expert && l % c.world == c.rank) {
+        if ((rc = src.experts(l, K_GATE, st->lo, st->n_local, L.gate, gate_b, s))) break;
+        if ((rc = src.experts(l, K_UP, st->lo, st->n_local, L.up, gate_b, s))) break;
+        if ((rc = src.experts(l, K_DOWN, st->lo, st->n_local, L.down, down_b, s))) break;
+        if (src.has_shared(l) && l % c.world == c.rank) {
             if ((rc = stack_alloc(st, &p, 2 * gate_b + down_b, "stack: shared expert"))) break;
             L.sh_gate = (uint8_t *)p;
             L.sh_up = L.sh_gate + gate_b;
             L.sh_down = L.sh_up + gate_b;
-            rc = bread_synth_blocks(L.sh_gate, (long long)(gate_b / Q4K_BYTES), BREAD_QTYPE_Q4_K, c.seed, sid(l, K_SH_GATE, 0), s);
-            if (!rc) rc = bread_synth_blocks(L.sh_up, (long long)(gate_b / Q4K_BYTES), BREAD_QTYPE_Q4_K, c.seed, sid(l, K_SH_UP, 0), s);
-            if (!rc) rc = bread_synth_blocks(L.sh_down, (long long)(down_b / Q6K_BYTES), BREAD_QTYPE_Q6_K, c.seed, sid(l, K_SH_DOWN, 0), s);
-            if (rc) break;
+            if ((rc = src.shared(l, K_SH_GATE, L.sh_gate, gate_b, s))) break;
+            if ((rc = src.shared(l, K_SH_UP, L.sh_up, gate_b, s))) break;
+            if ((rc = src.shared(l, K_SH_DOWN, L.sh_down, down_b, s))) break;
         }
         if ((rc = stack_alloc(st, &p, (size_t)E * H * 4 + (size_t)H * 2 + 256, "stack: router"))) break;
         L.W_r = (float *)p;
         L.w_sg = reinterpret_cast<__half *>((uint8_t *)p + (size_t)E * H * 4);
-        rc = bread_synth_normal_f32(L.W_r, (long long)E * H, 0.02f, c.seed, sid(l, K_ROUTER, 0), s);
-        if (!rc && c.shared_expert) rc = bread_synth_normal_f16(L.w_sg, H, 0.02f, c.seed, sid(l, K_SGVEC, 0), s);
-        if (!c.shared_expert) L.w_sg = nullptr;
-        if (rc) break;
+        if ((rc = src.router(l, L.W_r, (size_t)E * H, s))) break;
+        if (src.has_shared_gate(l)) {
+            if ((rc = src.shared_gate(l, L.w_sg, H, s))) break;
+        } else {
+            L.w_sg = nullptr;
+        }
+        if (src.has_norm(l)) {
+            if ((rc = stack_alloc(st, &p, (size_t)H * 4, "stack: norm weight"))) break;
+            L.norm_w = (float *)p;
+            if ((rc = src.norm(l, L.norm_w, H, s))) break;
+        }
         // pointer tables gate[E], up[E], down[E]; experts of other ranks are NULL
         std::vector<const uint8_t *> tab(3 * (size_t)E, nullptr);
         for (int j = 0; j < st->n_local; ++j) {
@@ -192,6 +368,7 @@ extern "C" int bread_stack_create(bread_stack_t **out, const bread_stack_config_
             d[l].sh_down = L.sh_down;
             d[l].W_r = L.W_r;
             d[l].w_sg = L.w_sg;
+            d[l].norm_w = L.norm_w;
         }
         void *p = nullptr;
         rc = stack_alloc(st, &p, d.size() * sizeof(StepLayer), "stack: layer descriptors");
@@ -218,7 +395,60 @@ extern "C" int bread_stack_create(bread_stack_t **out, const bread_stack_config_
     return BREAD_OK;
 }
 
+extern "C" int bread_stack_create(bread_stack_t **out, const bread_stack_config_t *cfg)
+{
+    if (!out || !cfg) return set_error(BREAD_ERR_ARG, "stack_create: NULL argument");
+    SynthSource src(*cfg);
+    return stack_build(out, *cfg, src);
+}
+
+extern "C" int bread_stack_create_gguf(bread_stack_t **out, const char *path, const bread_stack_config_t *cfg)
+{
+    if (!out || !path || !cfg) return set_error(BREAD_ERR_ARG, "stack_create_gguf: NULL argument");
+    *out = nullptr;
+    GgufSource src;
+    BREAD_TRY(bread_gguf_open(path, &src.g));
+    // shapes from layer 0's tensors: gate_exps [H, I, E] (dims[0] innermost), down_exps [I, H, E]
+    bread_gguf_tensor_t tg, td;
+    BREAD_TRY(src.need(0, "ffn_gate_exps", BREAD_QTYPE_Q4_K, &tg));
+    BREAD_TRY(src.need(0, "ffn_down_exps", BREAD_QTYPE_Q6_K, &td));
+    if (tg.n_dims != 3 || td.n_dims != 3 || td.dims[0] != tg.dims[1] || td.dims[1] != tg.dims[0] || td.dims[2] != tg.dims[2])
+        return set_error(BREAD_ERR_ARG, "stack_create_gguf: expert tensors of layer 0 have unexpected shapes");
+    bread_stack_config_t c = *cfg;
+    const int H = (int)tg.dims[0], I = (int)tg.dims[1], E = (int)tg.dims[2];
+    if ((c.hidden && c.hidden != H) || (c.inter && c.inter != I) || (c.n_experts && c.n_experts != E))
+        return set_error(BREAD_ERR_ARG, "stack_create_gguf: file has H=%d I=%d E=%d, config asks %d/%d/%d", H, I, E,
+                         c.hidden, c.inter, c.n_experts);
+    c.hidden = H;
+    c.inter = I;
+    c.n_experts = E;
+    c.shared_expert = src.has_shared(0) ? 1 : 0;
+    c.norm_weight = src.has_norm(0) ? 1 : 0;
+    if (cudaHostAlloc(&src.stage, GgufSource::STAGE, cudaHostAllocDefault) != cudaSuccess)
+        return set_error(BREAD_ERR_CUDA, "stack_create_gguf: pinned staging buffer");
+    return stack_build(out, c, src);
+}
+
 extern "C" size_t bread_stack_device_bytes(const bread_stack_t *st) { return st ? st->bytes : 0; }
+
+extern "C" int bread_stack_get_config(const bread_stack_t *st, bread_stack_config_t *out)
+{
+    if (!st || !out) return set_error(BREAD_ERR_ARG, "stack_get_config: NULL argument");
+    *out = st->cfg;
+    return BREAD_OK;
+}
+
+extern "C" int bread_stack_norm_weight(const bread_stack_t *st, int layer, float *host_out, int *has_weight)
+{
+    if (!st || layer < 0 || layer >= st->cfg.n_layers || !host_out || !has_weight)
+        return set_error(BREAD_ERR_ARG, "stack_norm_weight: bad argument");
+    const float *w = st->layers[layer].norm_w;
+    *has_weight = w ? 1 : 0;
+    if (w)
+        BREAD_CUDA(cudaMemcpy(host_out, w, (size_t)st->cfg.hidden * 4, cudaMemcpyDeviceToHost),
+                   "stack: read norm weight");
+    return BREAD_OK;
+}
 
 extern "C" int bread_stack_layer(const bread_stack_t *st, int layer, const void **gate_base, const void **up_base,
                                  const void **down_base, const float **W_r, const void **w_sg, const void **sh_gate,
@@ -256,6 +486,14 @@ extern "C" int bread_stack_set_peers(bread_stack_t *st, void *const *peer_mailbo
         st->peer_mb[r] = static_cast<float *>(peer_mailboxes[r]);
     }
     st->peers_set = true;
+    return BREAD_OK;
+}
+
+extern "C" int bread_stack_set_peer_timeout(bread_stack_t *st, double seconds)
+{
+    if (!st || !(seconds > 0.0) || seconds > 3600.0)
+        return set_error(BREAD_ERR_ARG, "stack_set_peer_timeout: seconds must be in (0, 3600]");
+    st->ep_wait_ns = (unsigned long long)(seconds * 1e9);
     return BREAD_OK;
 }
 
@@ -327,6 +565,7 @@ static int stack_launch(bread_stack_t *st, float *h, int T, cudaStream_t s, unsi
     a.out_per_layer = 1;
     st->rec_T = T;
     a.ep_world = c.world;
+    a.ep_wait_ns = st->ep_wait_ns;
     a.ep_rank = c.rank;
     a.ep_tmax = c.max_tokens;
     if (c.world > 1)

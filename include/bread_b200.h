@@ -174,6 +174,36 @@ int bread_moe_ffn_noalloc(const void *const *gate_ptrs, const void *const *up_pt
                           int *idx_out, float *w_out, float *sg_out, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------- */
+/* GGUF tensor index (gguf.c:306-411; host only)                           */
+/* ---------------------------------------------------------------------- */
+typedef struct bread_gguf bread_gguf_t;
+/* One tensor info record (gguf.h:80-88). */
+typedef struct bread_gguf_tensor {
+    const char *name;  /* owned by the open file */
+    uint32_t type;     /* ggml type id: 0 F32, 1 F16, 8 Q8_0, 12 Q4_K, 14 Q6_K ... */
+    uint32_t n_dims;
+    uint64_t dims[4];  /* dims[0] innermost (row length) */
+    uint64_t offset;   /* bytes from the start of the data section */
+    uint64_t size;     /* bytes of tensor data (0 for an unknown type) */
+    uint64_t n_elems;
+} bread_gguf_tensor_t;
+/* Opens a GGUF v2/v3 file and parses its header, metadata (keeping only
+ * general.alignment) and tensor index; no tensor data is read.  Replaces
+ * gguf_open (gguf.c:306-374), which exits on a malformed file: here any
+ * truncation or corruption returns BREAD_ERR_ARG. */
+int bread_gguf_open(const char *path, bread_gguf_t **out);
+int bread_gguf_close(bread_gguf_t *g);
+/* Header facts: version, tensor count, alignment, absolute data offset. */
+int bread_gguf_info(const bread_gguf_t *g, uint32_t *version, uint64_t *n_tensors, uint32_t *alignment,
+                    uint64_t *data_offset);
+/* Tensor info by index (gguf_tensor_by_idx, gguf.c:400-403) or by exact name
+ * (gguf_find_tensor, gguf.c:405-411; BREAD_ERR_ARG when absent). */
+int bread_gguf_tensor(const bread_gguf_t *g, uint64_t index, bread_gguf_tensor_t *out);
+int bread_gguf_find(const bread_gguf_t *g, const char *name, bread_gguf_tensor_t *out);
+/* Reads `bytes` from `offset` (relative to the data section) into host memory. */
+int bread_gguf_read(const bread_gguf_t *g, uint64_t offset, void *dst, uint64_t bytes);
+
+/* ---------------------------------------------------------------------- */
 /* Expert stack executor (the decode loop's MoE part, main.cu:683-687)     */
 /* ---------------------------------------------------------------------- */
 typedef struct bread_stack bread_stack_t;
@@ -190,8 +220,23 @@ typedef struct bread_stack_config {
     uint64_t seed;  /* synthetic weights: seeded generator (bread_synth_*) */
     int rank;       /* expert-parallel rank (0 for one GPU) */
     int world;      /* expert-parallel world size (1, 2, 4 or 8) */
+    int norm_weight; /* 1: each layer's RMSNorm multiplies by a weight vector
+                        (post_attention_norm.weight, one_layer.cu:1803-1818;
+                        synthetic: 1 + 0.1 N(0,1)); 0: unit weight */
 } bread_stack_config_t;
 
+/* The same stack with the weights of a GGUF model file (loader.c:156-206 and
+ * :628-693, which keep experts in a host LRU and stream them on demand; here
+ * every expert this rank holds is resident): per layer l < n_layers it reads
+ * blk.l.ffn_{gate,up,down}_exps.weight (Q4_K, Q4_K, Q6_K, experts outermost:
+ * this rank's experts are one contiguous byte range of each),
+ * blk.l.ffn_{gate,up,down}_shexp.weight (shared expert, if present),
+ * blk.l.ffn_gate_inp.weight (router, F32 [E x H]), blk.l.ffn_gate_inp_shexp.weight
+ * (shared gate, F16 [H], optional) and blk.l.post_attention_norm.weight (F32
+ * [H], optional).  hidden / inter / n_experts / shared_expert / norm_weight are
+ * taken from the file (cfg values must be 0 or match); seed is unused.  One
+ * device allocation per tensor kind per layer. */
+int bread_stack_create_gguf(bread_stack_t **out, const char *path, const bread_stack_config_t *cfg);
 /* Allocates and fills every weight this rank holds (experts [rank*E/world,
  * (rank+1)*E/world) of each layer, the router and shared-gate vector of every
  * layer, and the shared expert of the layers it owns), plus its scratch.
@@ -200,10 +245,17 @@ int bread_stack_create(bread_stack_t **out, const bread_stack_config_t *cfg);
 int bread_stack_destroy(bread_stack_t *st);
 /* Device bytes this rank holds (weights + scratch). */
 size_t bread_stack_device_bytes(const bread_stack_t *st);
+/* The configuration the stack was built with (for a GGUF stack: with the
+ * shapes and options read from the file). */
+int bread_stack_get_config(const bread_stack_t *st, bread_stack_config_t *out);
 /* Weights of one layer as device pointers (for parity checks). */
 int bread_stack_layer(const bread_stack_t *st, int layer, const void **gate_base, const void **up_base,
                       const void **down_base, const float **W_r, const void **w_sg, const void **sh_gate,
                       const void **sh_up, const void **sh_down, int *expert_lo, int *expert_hi);
+/* Copies the pre-MoE RMSNorm weight of one layer to host_out (fp32
+ * [hidden]); *has_weight = 0 (and nothing copied) when the stack normalises
+ * with unit weight.  Synchronous. */
+int bread_stack_norm_weight(const bread_stack_t *st, int layer, float *host_out, int *has_weight);
 /* Expert-parallel set-up (world > 1).  mailbox_bytes: size of the receive
  * mailbox this rank allocates (query with ptr = NULL).  bread_stack_mailbox
  * returns its device pointer; the caller exchanges CUDA IPC handles of every
@@ -211,6 +263,12 @@ int bread_stack_layer(const bread_stack_t *st, int layer, const void **gate_base
  * = own mailbox) to bread_stack_set_peers. */
 int bread_stack_mailbox(bread_stack_t *st, void **ptr, size_t *bytes);
 int bread_stack_set_peers(bread_stack_t *st, void *const *peer_mailboxes, int world);
+/* Bound of every device-side wait on another rank's data (default 20 s,
+ * because peers may start their launch late).  A wait that runs out sets the
+ * device error word (bread_device_error: bit 0) and every later wait on the
+ * device gives up at once, so the launch finishes with undefined h instead of
+ * hanging.  No reference counterpart (the reference runs on one GPU). */
+int bread_stack_set_peer_timeout(bread_stack_t *st, double seconds);
 /* CUDA IPC of a mailbox between the ranks' processes: 64-byte handle of a
  * device allocation; open a peer's handle (peer access enabled lazily); close
  * an opened mapping after bread_stack_destroy. */

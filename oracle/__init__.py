@@ -29,6 +29,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libbread_ref.so")
+REF_GPU_SO = os.path.join(HERE, "_ref", "libbread_refgpu.so")
 
 Q8_0, Q4_K, Q6_K = 8, 12, 14
 BLOCK_BYTES = {Q4_K: 144, Q6_K: 210, Q8_0: 34}
@@ -147,6 +148,27 @@ def ref() -> ctypes.CDLL:
         L.ref_max_threads.restype = _I
         _ref = L
     return _ref
+
+
+_refgpu = None
+
+
+def refgpu_available() -> bool:
+    return os.path.exists(REF_GPU_SO)
+
+
+def refgpu() -> ctypes.CDLL:
+    """The reference's own GPU GEMV (kernels.cu for sm_100a) with the
+    expert_bench.cu launch loop (ref_gpu_shim.cu): measurement only."""
+    global _refgpu
+    if _refgpu is None:
+        if not os.path.exists(REF_GPU_SO):
+            raise FileNotFoundError(f"{REF_GPU_SO} missing: build it with oracle.build() where the reference exists")
+        L = ctypes.CDLL(REF_GPU_SO)
+        L.refgpu_matvec.argtypes = [_P, _P, _P, _I, _I, _I, _P]
+        L.refgpu_expert_loop.argtypes = [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _P]
+        _refgpu = L
+    return _refgpu
 
 
 def _p(a: np.ndarray):
@@ -362,6 +384,40 @@ def ref_moe_block(es: ExpertSet, x, idx, wt, sg_weight, H: int, I: int, n_thread
     rc = ref().ref_moe_block(tg, tu, td, sgp, sup, sdp, _p(x), _p(idx), _p(wt), _p(sg), T, H, I, top_k,
                              n_threads, _p(out))
     assert rc == 0
+    return out
+
+
+class _RefGgufTensor(ctypes.Structure):
+    # gguf_tensor_t, gguf.h:80-88
+    _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_uint32), ("n_dims", ctypes.c_uint32),
+                ("dims", ctypes.c_uint64 * 4), ("offset", ctypes.c_uint64), ("size", ctypes.c_uint64),
+                ("n_elems", ctypes.c_uint64)]
+
+
+def ref_gguf_index(path: str) -> dict:
+    """The reference's own parser (gguf_open, gguf.c:306-374, compiled into
+    _ref/) on a well-formed file: version, data offset and every tensor info.
+    (It exits the process on a malformed file, so only valid files go here.)"""
+    L = ref()
+    L.gguf_open.restype = ctypes.c_void_p
+    L.gguf_open.argtypes = [ctypes.c_char_p]
+    L.gguf_close.argtypes = [ctypes.c_void_p]
+    L.gguf_version.restype = ctypes.c_uint32
+    L.gguf_version.argtypes = [ctypes.c_void_p]
+    L.gguf_num_tensors.restype = ctypes.c_uint64
+    L.gguf_num_tensors.argtypes = [ctypes.c_void_p]
+    L.gguf_data_offset.restype = ctypes.c_uint64
+    L.gguf_data_offset.argtypes = [ctypes.c_void_p]
+    L.gguf_tensor_by_idx.restype = ctypes.POINTER(_RefGgufTensor)
+    L.gguf_tensor_by_idx.argtypes = [ctypes.c_void_p, ctypes.c_uint64]
+    ctx = L.gguf_open(path.encode())
+    assert ctx, "reference gguf_open failed"
+    out = {"version": L.gguf_version(ctx), "data_offset": L.gguf_data_offset(ctx), "tensors": []}
+    for i in range(L.gguf_num_tensors(ctx)):
+        t = L.gguf_tensor_by_idx(ctx, i).contents
+        out["tensors"].append({"name": t.name.decode(), "type": t.type, "dims": list(t.dims[: t.n_dims]),
+                               "offset": t.offset, "size": t.size, "n_elems": t.n_elems})
+    L.gguf_close(ctx)
     return out
 
 

@@ -13,10 +13,12 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("world,T,port", [(2, 4, 29531), (2, 24, 29533)])
+@pytest.mark.parametrize("world,T,port", [(2, 1, 29529), (2, 4, 29531), (2, 24, 29533)])
 def test_ep_stack_matches_single_gpu(world, T, port):
-    """T=4: per-token routing tables; T=24: tiled router, shared ring arena and
-    grid-distributed top-k, with every rank routing all tokens."""
+    """T=1 and T=4: the flagged-word decode kernel on every rank, partials
+    exchanged as tagged words over NVLink; T=24: tiled router, shared ring
+    arena and grid-distributed top-k, arrival counters, with every rank
+    routing all tokens."""
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_T=str(T))
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={port}",
