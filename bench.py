@@ -716,6 +716,8 @@ def ep_parity(dist, rank: int, world: int, dev, seed: int) -> dict:
     for T in (1, 24):
         h0 = bb.synth_normal(T * H, 1.0, seed, 4242 + T, device=dev).view(T, H)
         h = h0.clone()
+        torch.cuda.synchronize()
+        dist.barrier()  # every rank launches the step together
         st.step(h)
         torch.cuda.synchronize()
         allh = [torch.empty_like(h) for _ in range(world)]

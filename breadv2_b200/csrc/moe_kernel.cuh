@@ -122,7 +122,7 @@ __device__ __forceinline__ void swait(uint64_t *bar, unsigned parity)
 // Flagged word *p once its tag equals `tag`: bounded poll (the grid-barrier
 // limit), giving up at once when a wait elsewhere on the device has failed.
 // Returns the payload (0 after a timeout, with the device error set).
-static __device__ __noinline__ uint32_t flagged_wait(const unsigned long long *p, uint32_t tag)
+static __device__ __noinline__ uint32_t flagged_wait(const unsigned long long *p, uint32_t tag, unsigned long long limit_ns)
 {
     unsigned long long t0 = 0;
     for (unsigned i = 0;; ++i) {
@@ -133,7 +133,7 @@ static __device__ __noinline__ uint32_t flagged_wait(const unsigned long long *p
             const unsigned long long now = globaltimer();
             if (!t0) {
                 t0 = now;
-            } else if (now - t0 > GRID_WAIT_NS) {
+            } else if (now - t0 > limit_ns) {
                 flag_error(DEVERR_TIMEOUT);
                 return 0u;
             }
@@ -143,9 +143,10 @@ static __device__ __noinline__ uint32_t flagged_wait(const unsigned long long *p
 }
 // Payload of an already loaded word, polling again only when its tag is not
 // the expected one (so a batch of loads is in flight together first).
-__device__ __forceinline__ uint32_t flagged_take(unsigned long long v, const unsigned long long *p, uint32_t tag)
+__device__ __forceinline__ uint32_t flagged_take(unsigned long long v, const unsigned long long *p, uint32_t tag,
+                                                  unsigned long long limit_ns)
 {
-    return (uint32_t)(v >> 32) == tag ? (uint32_t)v : flagged_wait(p, tag);
+    return (uint32_t)(v >> 32) == tag ? (uint32_t)v : flagged_wait(p, tag, limit_ns);
 }
 // The words addr(k), k < N with bit k of `valid` set, polled as one batch --
 // every word still carrying an old tag is loaded again in the same round --
@@ -217,6 +218,14 @@ __device__ __forceinline__ float tr_reduce(float (&v)[V])
     return v[0];
 }
 
+// Bound of the waits inside one GPU.  With expert parallelism every wait
+// depends, through the layers before it, on the other ranks' progress (a rank
+// may start its launch late), so all waits take the peer bound.
+__device__ __forceinline__ unsigned long long wait_bound(const StepArgs &a)
+{
+    return a.ep_world > 1 ? a.ep_wait_ns : GRID_WAIT_NS;
+}
+
 // Grid-wide barrier number `idx` of this launch (all 256 consumer threads).
 __device__ __forceinline__ void grid_barrier(const StepArgs &a, int idx, int tid)
 {
@@ -225,7 +234,7 @@ __device__ __forceinline__ void grid_barrier(const StepArgs &a, int idx, int tid
         // release at gpu scope, cumulative over the CTA's writes ordered by the
         // barrier above; the poll acquires
         red_release_gpu(a.ctrl + CTRL_GRID, 1ull);
-        wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(idx + 1) * gridDim.x, false, GRID_WAIT_NS);
+        wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(idx + 1) * gridDim.x, false, wait_bound(a));
     }
     named_sync(BAR_CONS, ST_CONS);
 }
@@ -399,7 +408,7 @@ __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *
         for (int j = 0; j < PER; ++j)
             if (lane + 32 * j < E) valid |= 1u << j;
         unsigned long long raw[PER + 1];
-        flagged_poll(raw, valid, [&](int k) { return k < PER ? row + lane + 32 * k : row + E; }, tag);
+        flagged_poll(raw, valid, [&](int k) { return k < PER ? row + lane + 32 * k : row + E; }, tag, wait_bound(a));
         for (int g = lane; g < HG; g += 32) ss += ssq_l[t * HG + g];
 #pragma unroll
         for (int j = 0; j < PER; ++j) p[j] = lane + 32 * j < E ? __uint_as_float((uint32_t)raw[j]) : -INFINITY;
@@ -487,14 +496,14 @@ __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *
 // routed experts held here, pairs token-major inside each group.
 // LLM: the logits come as flagged words (llg, tag) and, before anything else,
 // warp 0 waits for the presence word of every CTA for this layer (pres).
-template <int PER, bool BIG, bool LLM = false>
+template <int PER, bool BIG, bool LLM = false, bool T1 = false>
 __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const RouteTabs &R, int l, bool cta0,
                              unsigned long long *st, bool dist, const unsigned long long *llg = nullptr,
                              const unsigned long long *pres = nullptr, const float *ssq_l = nullptr,
                              uint32_t tag = 0)
 {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int T = a.T, E = a.E, K = a.top_k;
+    const int T = T1 ? 1 : a.T, E = a.E, K = a.top_k;
     const int EL = a.hi - a.lo;
     if constexpr (LLM) {
         if (warp == 0 && pres) {
@@ -504,7 +513,7 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
             for (int k = 0; k < LL_GMAX / 32; ++k)
                 if (lane + 32 * k < G) valid |= 1u << k;
             unsigned long long raw[LL_GMAX / 32];
-            flagged_poll(raw, valid, [&](int k) { return pres + lane + 32 * k; }, tag);
+            flagged_poll(raw, valid, [&](int k) { return pres + lane + 32 * k; }, tag, wait_bound(a));
         }
     }
     for (int i = tid; i < EL; i += ST_CONS) {
@@ -799,12 +808,16 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
 // them in rank order (so every rank holds the same bits and routes the same):
 // no arrival counters, no system-scope release, no grid barrier.
 constexpr int MODE_LL = 0, MODE_SMALL = 1, MODE_BIG = 2, MODE_LLEP = 3;
-template <int NBH, int NBI, int MODE>
+// T1: the decode modes compiled for exactly one token (the batch-1 decode
+// step): every per-token loop and the batch paths of the routing drop out of
+// the instruction stream, which is on this latency-bound step's critical path.
+template <int NBH, int NBI, int MODE, bool T1 = false>
 __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_constant__ StepArgs a)
 {
     constexpr bool BIG = MODE == MODE_BIG;
     constexpr bool LL = MODE == MODE_LL || MODE == MODE_LLEP;
     constexpr bool LLEP = MODE == MODE_LLEP;
+    static_assert(!T1 || LL, "the one-token instantiation is a decode mode");
     using C = SCfg<NBH, NBI>;
     using GH = typename C::GH;
     using GI = typename C::GI;
@@ -813,7 +826,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
     const StepSmem &m = a.sm;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, bx = blockIdx.x;
-    const int T = a.T, E = a.E;
+    const int T = T1 ? 1 : a.T, E = a.E;
     const int TC = T < MOE_TC ? T : MOE_TC;
     const int R = I / MOE_ROWTILE;  // gate/up row tiles per expert
     const int NT = H / MOE_RT3;     // 16-column tiles of h (down output)
@@ -843,6 +856,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
     RT.scal = reinterpret_cast<int *>(smem + m.r_scal);
     RT.ptr = reinterpret_cast<const uint8_t **>(smem + m.r_ptr);
     RT.chunk = reinterpret_cast<int4 *>(smem + m.r_chunk);
+    // chunk c of the routing tables (one token: always one pair)
+    auto cinfo = [&](int c) {
+        ChunkInfo ci = chunk_info(RT, c);
+        if (T1) ci.np = 1;
+        return ci;
+    };
     uint8_t *xsl = smem + m.xsl;
     uint8_t *gring = smem + m.gring;
     float *abuf = reinterpret_cast<float *>(smem + m.abuf);
@@ -983,7 +1002,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             // tokens + 32 gate and up rows in sub-stages
             for (int it = bx; it < nch * R; it += G, ++nX) {
                 const int c = it / R, rt = it % R;  // R: a power of two
-                const ChunkInfo ci = chunk_info(RT, c);
+                const ChunkInfo ci = cinfo(c);
                 if constexpr (!LL) {  // (flagged mode: every CTA quantised the input itself)
                     const int xs_ = nX & 1;
                     if (lane == 0) {
@@ -1021,7 +1040,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             const int dpre = arena ? 0 : (nds < NS_D ? nds : NS_D);
             auto issue_dw = [&](const Ring &d, int n) {
                 if (d.used) swait(dempty + d.slot, (unsigned)(d.phase ^ 1));
-                const ChunkInfo ci = chunk_info(RT, n % nch);
+                const ChunkInfo ci = cinfo(n % nch);
                 const int it3 = bx + (n / nch) * G;
                 const uint8_t *db = mat_ptr(RT, Ld, a, ci.e, 2);
                 if (db && !(reinterpret_cast<uintptr_t>(db) & 15)) {
@@ -1034,18 +1053,17 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 }
             };
             auto issue_da = [&](const Ring &d, int n) {
-                const ChunkInfo ci = chunk_info(RT, n % nch);
+                const ChunkInfo ci = cinfo(n % nch);
                 uint8_t *st = dring + (size_t)d.slot * m.dslot + C::WB;
                 mbar_arrive_expect_tx(da + d.slot, (unsigned)(ci.np * C::ATOK));
                 bulk_g2s(st, a.aq + (size_t)ci.p0 * I, (unsigned)(ci.np * I * 2), da + d.slot);
                 bulk_g2s(st + (size_t)TC * I * 2, a.as + (size_t)ci.p0 * (I / 32), (unsigned)(ci.np * (I / 8)),
                          da + d.slot);
             };
-            if (l + 1 < a.L) issue_router(l + 1);  // consumers are past phase A
-            pstamp(l, 13);
             // The down weights are needed only after the next grid barrier:
             // request them once this CTA's gate/up stages have landed, so they
-            // do not compete with them for HBM.
+            // do not compete with them for HBM (nor do the next layer's router
+            // rows, issued with them).
             if (dpre > 0 && nch * R > bx) {
                 if (lane < C::SPI && lane < NS_G) {
                     // stage issued `lane + 1` positions before the cursor: its slot
@@ -1058,12 +1076,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             if (lane < dpre) issue_dw(dR.ahead(lane, NS_D), lane);
             __syncwarp();
             pstamp(l, 12);
+            if (l + 1 < a.L) issue_router(l + 1);  // consumers are past phase A
+            pstamp(l, 13);
             // the intermediate of every CTA is complete after grid barrier (phase
             // B); flagged mode: the consumers gather it themselves
             if constexpr (!LL) {
                 if (lane == 0) {
                     const int bidx = l * nbl + (dist ? 2 : 1);
-                    wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(bidx + 1) * G, false, GRID_WAIT_NS);
+                    wait_counter(a.ctrl + CTRL_GRID, (unsigned long long)(bidx + 1) * G, false, wait_bound(a));
                 }
                 __syncwarp();
                 fence_proxy_async_global();
@@ -1171,7 +1191,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     for (int k = 0; k < 8; ++k)
                         if (i0 + k * ST_CONS < n) valid |= 1u << k;
                     unsigned long long r[8];
-                    flagged_poll(r, valid, [&](int k) { return hin + i0 + k * ST_CONS; }, tgp);
+                    flagged_poll(r, valid, [&](int k) { return hin + i0 + k * ST_CONS; }, tgp, wait_bound(a));
 #pragma unroll
                     for (int k = 0; k < 8; ++k)
                         if ((valid >> k) & 1u) xf[i0 + k * ST_CONS] = __uint_as_float((uint32_t)r[k]);
@@ -1410,7 +1430,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             const unsigned long long *pres =
                 (LL && E + (Ld.w_sg ? 1 : 0) < G) ? a.ll_pres + par_of(l) * a.ll_pres_n : nullptr;
             if (LL || E <= 256)  // (decode mode is used only with E <= 256)
-                route_tables<8, BIG, LL>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql, tg);
+                route_tables<8, BIG, LL, T1>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql, tg);
             else
                 route_tables<MOE_EMAX / 32, BIG, LL>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql, tg);
         }
@@ -1425,7 +1445,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             XSlice X[GH::CP];
             for (int it = bx; it < nch * R; it += G, ++nX) {
                 const int c = it / R, rt = it % R;  // R: a power of two
-                const ChunkInfo ci = chunk_info(RT, c);
+                const ChunkInfo ci = cinfo(c);
                 const int xs_ = nX & 1;
                 if constexpr (!LL) swait(xfull + xs_, (unsigned)((nX >> 1) & 1));
                 if (stamp && it == bx) stamp_at(l, 4);
@@ -1582,7 +1602,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     flagged_poll(r, valid, [&](int k) {
                         const int i = i0 + k * ST_CONS;
                         return i < na ? fa + i : fs + (i - na);
-                    }, tg);
+                    }, tg, wait_bound(a));
 #pragma unroll
                     for (int k = 0; k < 16; ++k) {
                         const int i = i0 + k * ST_CONS;
@@ -1606,7 +1626,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     if (ep || i >= T * MOE_RT3)
                         rv[k] = 0.0f;
                     else if (fres)
-                        rv[k] = __uint_as_float(flagged_take(ld_flagged(fres + o), fres + o, tag_of(l - 1)));
+                        rv[k] = __uint_as_float(flagged_take(ld_flagged(fres + o), fres + o, tag_of(l - 1), wait_bound(a)));
                     else
                         rv[k] = __ldcg(res + o);
                 }
@@ -1630,7 +1650,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                         swait(dw + slot, par);
                         if constexpr (!LL) swait(da + slot, par);
                         if (stamp && s == 0 && it3 == bx) stamp_at(l, 7);
-                        const ChunkInfo ci = chunk_info(RT, c);
+                        const ChunkInfo ci = cinfo(c);
                         const int16_t *aqs = LL ? alq + (size_t)ci.p0 * I : reinterpret_cast<const int16_t *>(st + C::WB);
                         const float *ass = LL ? als + (size_t)ci.p0 * (I / 32)
                                               : reinterpret_cast<const float *>(st + C::WB + (size_t)TC * I * 2);
@@ -1692,7 +1712,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                     swait(dw + slot, par);
                     if constexpr (!LL) swait(da + slot, par);
                     if (stamp && r0 == 0 && it3 == bx) stamp_at(l, 7);
-                    const ChunkInfo ci = chunk_info(RT, c);
+                    const ChunkInfo ci = cinfo(c);
                     const int16_t *aqs = LL ? alq + (size_t)ci.p0 * I : reinterpret_cast<const int16_t *>(st + C::WB);
                     const float *ass = LL ? als + (size_t)ci.p0 * (I / 32)
                                           : reinterpret_cast<const float *>(st + C::WB + (size_t)TC * I * 2);
@@ -1933,11 +1953,13 @@ static int setup_nb()
     if (dev < 0 || dev >= MAX_DEVICES) return set_error(BREAD_ERR_STATE, "moe step: device %d", dev);
     std::lock_guard<std::mutex> lock(mu);
     if (!done[dev]) {
-        for (int mode = 0; mode < 4; ++mode) {
+        for (int mode = 0; mode < 6; ++mode) {
             auto kern = mode == MODE_LL      ? moe_step_kernel<NBH, NBI, MODE_LL>
                         : mode == MODE_SMALL ? moe_step_kernel<NBH, NBI, MODE_SMALL>
                         : mode == MODE_BIG   ? moe_step_kernel<NBH, NBI, MODE_BIG>
-                                             : moe_step_kernel<NBH, NBI, MODE_LLEP>;
+                        : mode == MODE_LLEP  ? moe_step_kernel<NBH, NBI, MODE_LLEP>
+                        : mode == 4          ? moe_step_kernel<NBH, NBI, MODE_LL, true>
+                                             : moe_step_kernel<NBH, NBI, MODE_LLEP, true>;
             BREAD_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_LIMIT),
                        "moe step: shared-memory attribute");
             int n = 0;
@@ -1985,8 +2007,12 @@ static int launch_nb(StepArgs &a, cudaStream_t s)
         BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_BIG>, a), "moe step launch");
     else if (mode == MODE_SMALL)
         BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_SMALL>, a), "moe step launch");
+    else if (mode == MODE_LLEP && a.T == 1)
+        BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_LLEP, true>, a), "moe step launch");
     else if (mode == MODE_LLEP)
         BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_LLEP>, a), "moe step launch");
+    else if (a.T == 1)
+        BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_LL, true>, a), "moe step launch");
     else
         BREAD_CUDA(cudaLaunchKernelEx(&cfg, moe_step_kernel<NBH, NBI, MODE_LL>, a), "moe step launch");
     return BREAD_OK;
