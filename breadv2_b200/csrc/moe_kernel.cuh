@@ -1402,11 +1402,29 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             // out: it overlaps the wait for the other CTAs' logits.  One token:
             // warp 0 routes meanwhile (warps 1..7 quantise); the routing's
             // consumer barriers publish the values before any gate/up item.
-            const int w0 = T == 1 ? 1 : 0, nw = 8 - w0;
-            for (int gi = warp - w0; warp >= w0 && gi < T * (H / 32); gi += nw) {
-                const int q = quant32(xf[gi * 32 + lane], xls + gi, lane);
-                const int e = gi * 32 + lane, t = e / H;  // H: a power of two
-                xlq[(size_t)t * H + xq_pos(e - t * H)] = (int16_t)q;
+            const int w0 = T == 1 ? 1 : 0, nw = 8 - w0, ngq = T * (H / 32);
+            if (warp >= w0) {
+                // four groups per round (groups warp - w0 + nw * m), their
+                // reductions interleaved
+                for (int m0 = 0; warp - w0 + nw * m0 < ngq; m0 += 4) {
+                    float v[4], sc[4];
+                    int q[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int gi = warp - w0 + nw * (m0 + k);
+                        v[k] = gi < ngq ? xf[gi * 32 + lane] : 0.0f;
+                    }
+                    quant32_n<4>(v, q, sc);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int gi = warp - w0 + nw * (m0 + k);
+                        if (gi < ngq) {
+                            const int e = gi * 32 + lane, t = e / H;  // H: a power of two
+                            xlq[(size_t)t * H + xq_pos(e - t * H)] = (int16_t)q[k];
+                            if (lane == 0) xls[gi] = sc[k];
+                        }
+                    }
+                }
             }
         }
         if (stamp) stamp_at(l, 1);

@@ -98,6 +98,30 @@ __device__ __forceinline__ int quant32(float v, float *scale, int lane)
     return q;
 }
 
+// N groups at once (one value of each per lane), the same arithmetic per
+// group as quant32, their reductions interleaved: q[k] and the scale sc[k]
+// (valid on every lane) of group k.
+template <int N>
+__device__ __forceinline__ void quant32_n(const float (&v)[N], int (&q)[N], float (&sc)[N])
+{
+    float a[N];
+    bool finite[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+        a[k] = fabsf(v[k]);
+        finite[k] = !__any_sync(0xffffffffu, !(a[k] <= 3.402823466e38f));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+#pragma unroll
+        for (int k = 0; k < N; ++k) a[k] = fmaxf(a[k], __shfl_xor_sync(0xffffffffu, a[k], o));
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+        q[k] = (a[k] > 0.0f && finite[k]) ? __float2int_rn((v[k] / a[k]) * 32767.0f) : 0;
+        sc[k] = finite[k] ? a[k] * (1.0f / 32767.0f) : __int_as_float(0x7fc00000);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // lane dots
 // ---------------------------------------------------------------------------

@@ -59,7 +59,10 @@ def test_mangled_glue_launchers(cuda):
 
     d = torch.randn(2048, device=cuda).half()
     src = torch.randn(2048, device=cuda).half()
-    ref = (d.float() + 0.37 * src.float()).half()
+    # the kernel (like the reference's nvcc build) fuses the multiply-add: one
+    # fp32 rounding of the exact d + c*s (exact in fp64), then fp16
+    c = torch.tensor(0.37, dtype=torch.float32).double()
+    ref = (d.double() + c * src.double()).float().half()
     out = d.clone()
     _sym("bread_scale_accum")(P(out.data_ptr()), P(src.data_ptr()), ctypes.c_float(0.37), 2048, s)
     torch.cuda.synchronize()

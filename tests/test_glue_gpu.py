@@ -26,7 +26,10 @@ def test_silu_mul(cuda):
 def test_scale_accum(cuda):
     d = torch.randn(2048, device=cuda).half()
     s = torch.randn(2048, device=cuda).half()
-    ref = (d.float() + 0.37 * s.float()).half()
+    # fused multiply-add as the kernel (and the reference's nvcc build): one fp32
+    # rounding of the exact d + c*s (exact in fp64), then fp16
+    c = torch.tensor(0.37, dtype=torch.float32).double()
+    ref = (d.double() + c * s.double()).float().half()
     out = d.clone()
     bb.scale_accum(out, s, 0.37)
     assert ulp_close(out, ref)
