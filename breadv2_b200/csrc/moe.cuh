@@ -55,7 +55,8 @@ static_assert(sizeof(StepLayer) % 8 == 0, "layer descriptors are copied to share
 // Control words at the head of the workspace (u64 each): the grid-barrier
 // counter, the exit ticket, the launch epoch and the layer sequence (tags of
 // the flagged exchange words, below).  Zero before the first launch; the last
-// CTA of every launch resets the first two, advances the epoch by one and the
+// CTA of every launch resets the first two, advances the epoch by one if the
+// launch counted expert-parallel arrivals in the mailbox counters, and the
 // layer sequence by the launch's layers.
 enum { CTRL_GRID = 0, CTRL_EXIT = 1, CTRL_EPOCH = 2, CTRL_SEQ = 3 };
 

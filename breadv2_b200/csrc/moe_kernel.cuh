@@ -390,11 +390,16 @@ __device__ __forceinline__ ChunkInfo chunk_search(const RouteTabs &R, int c)
 // LLM (flagged-exchange mode): the logits (row E = the shared-gate score) are
 // flagged words at llg [t * (E + 1) + row] with tag `tag`, and the group sums
 // of squares sit in shared memory (ssq_l), computed by this CTA.
-template <int PER, bool LLM = false>
+struct NoEarly {
+    __device__ void operator()(int) const {}
+};
+// `early(e)` runs (all lanes) as soon as pick number `kw` is known.
+template <int PER, bool LLM = false, class Early = NoEarly>
 __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *idx, float *w, float *rinv,
                             float *sgw, bool outputs, unsigned long long *st, int l, int *pick_i = nullptr,
                             float *pick_w = nullptr, float *pick_sg = nullptr,
-                            const unsigned long long *llg = nullptr, const float *ssq_l = nullptr, uint32_t tag = 0)
+                            const unsigned long long *llg = nullptr, const float *ssq_l = nullptr, uint32_t tag = 0,
+                            int kw = -1, const Early &early = Early{})
 {
     const int lane = threadIdx.x & 31;
     const int H = a.H, E = a.E, K = a.top_k, HG = H / 32;
@@ -450,6 +455,7 @@ __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *
         for (int j = PER - 1; j >= 0; --j)
             if (key[j] == mk) cand = (unsigned)(lane + 32 * j);
         const unsigned bi = __reduce_min_sync(0xffffffffu, cand);
+        if (k == kw) early((int)bi);
         if ((int)(bi & 31) == lane) {
 #pragma unroll
             for (int j = 0; j < PER; ++j)
@@ -496,11 +502,11 @@ __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *
 // routed experts held here, pairs token-major inside each group.
 // LLM: the logits come as flagged words (llg, tag) and, before anything else,
 // warp 0 waits for the presence word of every CTA for this layer (pres).
-template <int PER, bool BIG, bool LLM = false, bool T1 = false>
+template <int PER, bool BIG, bool LLM = false, bool T1 = false, class Early = NoEarly>
 __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const RouteTabs &R, int l, bool cta0,
                              unsigned long long *st, bool dist, const unsigned long long *llg = nullptr,
                              const unsigned long long *pres = nullptr, const float *ssq_l = nullptr,
-                             uint32_t tag = 0)
+                             uint32_t tag = 0, int kw = -1, const Early &early = Early{})
 {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = T1 ? 1 : a.T, E = a.E, K = a.top_k;
@@ -536,8 +542,8 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
         if (warp == 0) {
             int e;
             float w, sg;
-            route_token<PER, LLM>(a, Ld, 0, R.idx, R.w, R.rinv, R.sgw, cta0, (st && lane == 0) ? st : nullptr, l, &e,
-                                  &w, &sg, llg, ssq_l, tag);
+            route_token<PER, LLM, Early>(a, Ld, 0, R.idx, R.w, R.rinv, R.sgw, cta0, (st && lane == 0) ? st : nullptr,
+                                         l, &e, &w, &sg, llg, ssq_l, tag, kw, early);
             const int hs = Ld.sh_gate ? 1 : 0;
             const bool loc = lane < K && e >= a.lo && e < a.hi;
             const unsigned locs = __ballot_sync(0xffffffffu, loc);
@@ -993,6 +999,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         for (int l = 0; l < a.L; ++l) {
             named_sync(BAR_ALL, ST_THREADS);  // routing tables of layer l are ready
             if (a.route_only) break;
+            if (T1 && RT.scal[3] > 0) npre = RT.scal[3];  // issued by the routing warp at its pick
             pstamp(l, 10);
             const StepLayer Ld = layer_desc(a, l);
             // (the copies below read data other CTAs wrote only in barrier modes)
@@ -1447,7 +1454,42 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             const unsigned long long *llg = LL ? a.ll_lg + par_of(l) * a.ll_lg_n : nullptr;
             const unsigned long long *pres =
                 (LL && E + (Ld.w_sg ? 1 : 0) < G) ? a.ll_pres + par_of(l) * a.ll_pres_n : nullptr;
-            if (LL || E <= 256)  // (decode mode is used only with E <= 256)
+            if constexpr (T1) {
+                // One token: the routing warp requests this CTA's first gate/up
+                // item itself as soon as the item's expert is picked (pick
+                // bx / R - shared, in top-k order: the order of the chunks),
+                // into the ring positions the producer would use next (the
+                // consumers' cursor mirrors it; the slots' previous uses ended
+                // in the last layer's item loop, which every consumer warp has
+                // left), and tells the producer how many sub-stages to skip.
+                const int hs = Ld.sh_gate ? 1 : 0, c0 = bx / R;
+                // (one GPU only: with expert parallelism the chunks follow the
+                // rank's own picks, not the top-k order)
+                const int kw = (Ld.gate_base && a.ep_world == 1 && c0 >= hs && c0 < hs + a.top_k) ? c0 - hs : -1;
+                if (warp == 0 && lane == 0) RT.scal[3] = 0;
+                auto early = [&](int e) {
+                    if (e < a.lo || e >= a.hi) return;
+                    const int n = C::SPI < NS_G ? C::SPI : NS_G;
+                    const size_t j = (size_t)(e - a.lo);
+                    const uint8_t *gb = Ld.gate_base + j * Ld.gu_stride, *ub = Ld.up_base + j * Ld.gu_stride;
+                    if (lane < n) {
+                        const Ring g = gR.ahead(lane, NS_G);
+                        const unsigned bytes = (unsigned)(C::SR * GH::ROWB);
+                        const size_t r0 = (size_t)(bx % R) * MOE_ROWTILE + (size_t)lane * C::SR;
+                        uint8_t *dst = gring + (size_t)g.slot * C::STB;
+                        if (!((reinterpret_cast<uintptr_t>(gb) | reinterpret_cast<uintptr_t>(ub)) & 15)) {
+                            mbar_arrive_expect_tx(gfull + g.slot, 2 * bytes);
+                            bulk_g2s(dst, gb + r0 * GH::ROWB, bytes, gfull + g.slot);
+                            bulk_g2s(dst + bytes, ub + r0 * GH::ROWB, bytes, gfull + g.slot);
+                        } else {
+                            flag_error(DEVERR_ROUTE);
+                            mbar_arrive(gfull + g.slot);
+                        }
+                    }
+                    if (lane == 0) RT.scal[3] = n;
+                };
+                route_tables<8, BIG, LL, T1>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql, tg, kw, early);
+            } else if (LL || E <= 256)  // (decode mode is used only with E <= 256)
                 route_tables<8, BIG, LL, T1>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql, tg);
             else
                 route_tables<MOE_EMAX / 32, BIG, LL>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql, tg);
@@ -1843,7 +1885,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             }
     }
 
-    // exit ticket: the last CTA re-arms the barrier counter and advances the epoch
+    // exit ticket: the last CTA re-arms the barrier counter, advances the epoch
+    // (counter-mode launches) and the layer sequence
     named_sync(BAR_CONS, ST_CONS);
     if (tid == 0) {
         __threadfence();
@@ -1851,7 +1894,10 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
         if (prev == (unsigned long long)G - 1) {
             a.ctrl[CTRL_GRID] = 0;
             a.ctrl[CTRL_EXIT] = 0;
-            a.ctrl[CTRL_EPOCH] = epoch + 1;
+            // the epoch counts the launches that add arrivals to the mailbox
+            // counters (the targets derive from it); decode launches with
+            // expert parallelism exchange tagged words and add none
+            a.ctrl[CTRL_EPOCH] = ep ? epoch + 1 : epoch;
             a.ctrl[CTRL_SEQ] = seq0 + (unsigned long long)a.L;
             __threadfence();
         }

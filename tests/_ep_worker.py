@@ -20,16 +20,21 @@ def main():
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
     T = int(os.environ.get("EP_T", "4"))
     cfg = dict(n_layers=int(os.environ.get("EP_LAYERS", "3")), hidden=1024, inter=512, n_experts=32, top_k=4,
-               max_tokens=max(8, T), shared_expert=True, norm_eps=1e-6, seed=21)
+               max_tokens=max(8, T, int(os.environ.get("EP_MIX", "0"))), shared_expert=True, norm_eps=1e-6, seed=21)
     st = bb.ExpertStack(**cfg, rank=rank, world=world)
     st.connect_peers(dist)
     h0 = bb.synth_normal(T * 1024, 1.0, 21, 7, device="cuda").view(T, 1024)
     outs = []
+    mix = int(os.environ.get("EP_MIX", "0"))  # a step of MIX tokens between the replays
     for _ in range(3):  # replays reuse the mailbox slots
         h = h0.clone()
         st.step(h)
         torch.cuda.synchronize()
         outs.append(h.cpu())
+        if mix:
+            hm = bb.synth_normal(mix * 1024, 1.0, 21, 8, device="cuda").view(mix, 1024)
+            st.step(hm)
+            torch.cuda.synchronize()
     err = bb.device_error()
     same_replay = all(torch.equal(outs[0], o) for o in outs[1:])
     gathered = [None] * world

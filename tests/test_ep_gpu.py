@@ -13,13 +13,16 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("world,T,port", [(2, 1, 29529), (2, 4, 29531), (2, 24, 29533)])
-def test_ep_stack_matches_single_gpu(world, T, port):
+@pytest.mark.parametrize("world,T,mix,port", [(2, 1, 0, 29529), (2, 4, 0, 29531), (2, 24, 0, 29533), (2, 1, 24, 29535),
+                                              (2, 24, 1, 29537)])
+def test_ep_stack_matches_single_gpu(world, T, mix, port):
     """T=1 and T=4: the flagged-word decode kernel on every rank, partials
     exchanged as tagged words over NVLink; T=24: tiled router, shared ring
     arena and grid-distributed top-k, arrival counters, with every rank
-    routing all tokens."""
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_T=str(T))
+    routing all tokens.  mix: a step of that many tokens between the replays
+    on the same stack (decode steps exchange tagged words, batched steps count
+    arrivals: each must leave the other's state intact)."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_T=str(T), EP_MIX=str(mix))
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={port}",
            os.path.join(HERE, "_ep_worker.py")]
