@@ -534,10 +534,17 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     # The step is ONE kernel launch (moe_step_kernel): achieved = algorithmic
     # bytes of the step / its CUDA-event duration from the timed loop.
     achieved = step_bytes / (ms_step * 1e-3) / 1e9
-    # instantiation that runs: 0 = flagged-word decode (one GPU, T <= 8),
-    # 1 = grid barriers at T <= 8 (expert parallel), 2 = T > 8
-    mode = 2 if T > 8 else (0 if world == 1 and os.environ.get("BREAD_NO_FLAGGED") != "1" else 1)
-    kname = f"moe_step_kernel<{H // 256},{I // 256},{mode}>"
+    # instantiation that runs: 0 = tagged-word decode on one GPU (T <= 8),
+    # 1 = grid barriers at T <= 8 (BREAD_NO_FLAGGED=1), 2 = T > 8,
+    # 3 = tagged-word decode with expert parallelism; one-token launches of
+    # modes 0 and 3 use the one-token instantiation (fourth argument true)
+    if T > 8:
+        mode = 2
+    elif os.environ.get("BREAD_NO_FLAGGED") == "1":
+        mode = 1
+    else:
+        mode = 3 if world > 1 else 0
+    kname = f"moe_step_kernel<{H // 256},{I // 256},{mode}{',true' if T == 1 and mode in (0, 3) else ''}>"
     traffic = None
     tfile = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tfile):
