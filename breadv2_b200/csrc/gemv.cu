@@ -10,13 +10,18 @@
 //     covers 32/(4*cols/256) rows per step;
 //   * the activation is quantised once per CTA to int16 per 32 values and
 //     each lane keeps its 64-value slice in registers (one token) or reloads
-//     it from shared memory per token (several tokens);
+//     it from shared memory per token (several tokens); a group whose largest
+//     value dwarfs the rest also gets a second int16 level (the first level's
+//     error, quant32_r_n), and when any group of the launch has one, every row
+//     takes a second dot pass over that residual (exact by linearity);
 //   * weight x activation products are exact int32 dp2a sums per sub-block,
 //     scaled in fp32 (qdot.cuh).
 // Generic path (any alignment, any cols multiple of the block, Q8_0): one warp
 // per row, exact fp32 dequantisation per element, fp32 FMA.
 #include <stdio.h>
 #include <stdlib.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "ptx.cuh"
@@ -39,6 +44,9 @@ struct Geo {
 constexpr int GEMV_WARPS = 8;
 constexpr int GEMV_STAGES = 3;   // shared-memory stages per warp
 constexpr int GEMV_TMAX = 8;     // tokens per launch on the fast path
+// tokens per launch at NB super-blocks per row: at 4096 columns eight tokens'
+// two activation levels would not fit in shared memory beside the stages
+__host__ __device__ constexpr int gemv_tmax(int nb) { return nb >= 16 ? 4 : GEMV_TMAX; }
 
 // warp steps per bulk copy: copies of about 2.3 - 3.5 KB
 template <int STEPB>
@@ -48,37 +56,86 @@ struct Chunk {
 
 __host__ __device__ constexpr size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Shared-memory offsets of a launch of T tokens: per level (first, then the
+// residual) int16 values [T x cols] in the xq_pos layout, fp32 scales per 32
+// and int sums per 16; then the per-warp stages and their mbarriers.
+struct GemvLayout {
+    size_t xs, xs16, xr, xs2, xr16, st;
+    __host__ __device__ GemvLayout(int T, int cols)
+    {
+        const size_t q = align_up((size_t)T * cols * 2, 16), s = align_up((size_t)T * cols / 32 * 4, 16),
+                     s16 = align_up((size_t)T * cols / 16 * 4, 16);
+        xs = q;
+        xs16 = xs + s;
+        xr = xs16 + s16;
+        xs2 = xr + q;
+        xr16 = xs2 + s;
+        st = xr16 + s16;
+    }
+};
+
 template <int QT, int NB>
 struct GemvSmem {
     static constexpr int CH = Chunk<Geo<QT, NB>::STEPB>::CH;
     static constexpr size_t chunk = (size_t)Geo<QT, NB>::STEPB * CH;
-    static size_t bytes(int T)
+    // prow: rows per warp of the two-pass row values
+    static size_t bytes(int T, int prow)
     {
-        size_t b = align_up((size_t)T * Geo<QT, NB>::COLS * 2, 16);           // xq
-        b += align_up((size_t)T * Geo<QT, NB>::COLS / 32 * 4, 16);             // xs
-        b += align_up((size_t)T * Geo<QT, NB>::COLS / 16 * 4, 16);             // xs16
+        size_t b = GemvLayout(T, Geo<QT, NB>::COLS).st;
         b += (size_t)GEMV_WARPS * GEMV_STAGES * chunk + 16;                    // stages + tail pad
         b = align_up(b, 8) + GEMV_WARPS * GEMV_STAGES * 8;                     // mbarriers
+        b = align_up(b, 16) + (size_t)GEMV_WARPS * prow * T * 4;               // row values
         return b;
     }
 };
 
-// Quantise T x cols activations (fp32 or fp16) into shared memory.
+// Quantise T x cols activations (fp32 or fp16) into shared memory, both
+// levels, four groups per warp at a time (their reductions interleaved);
+// returns nonzero on the lanes of a warp that gave some group a second level.
 template <bool IN_HALF>
-__device__ __forceinline__ void quantise_to_smem(const void *x, int T, int cols, int16_t *xq, float *xs, int *xs16,
-                                                 int warp, int nwarps, int lane)
+__device__ __forceinline__ int quantise_to_smem(const void *x, int T, int cols, int16_t *xq, float *xs, int *xs16,
+                                                int16_t *xr, float *xs2, int *xr16, int warp, int nwarps, int lane)
 {
+    constexpr int N = 4;
     const int groups = T * cols / 32;
-    for (int gi = warp; gi < groups; gi += nwarps) {
-        const int idx = gi * 32 + lane;
-        const float v = IN_HALF ? __half2float(reinterpret_cast<const __half *>(x)[idx])
+    int two = 0;
+    for (int g0 = warp; g0 < groups; g0 += N * nwarps) {
+        float v[N];
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            const int gi = g0 + k * nwarps;
+            const int idx = gi * 32 + lane;
+            v[k] = gi >= groups ? 0.0f
+                   : IN_HALF    ? __half2float(reinterpret_cast<const __half *>(x)[idx])
                                 : reinterpret_cast<const float *>(x)[idx];
-        const int q = quant32(v, xs + gi, lane);
-        const int t = idx / cols, e = idx - t * cols;
-        xq[(size_t)t * cols + xq_pos(e)] = (int16_t)q;
-        const int s16 = sum16(q);
-        if ((lane & 15) == 0) xs16[2 * gi + (lane >> 4)] = s16;
+        }
+        int q[N], r[N];
+        float sc[N], s2[N];
+        quant32_r_n<N>(v, q, r, sc, s2);
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            const int gi = g0 + k * nwarps;
+            if (gi >= groups) break;  // (warp-uniform)
+            const int idx = gi * 32 + lane;
+            const int t = idx / cols, e = idx - t * cols;
+            xq[(size_t)t * cols + xq_pos(e)] = (int16_t)q[k];
+            const int s16 = sum16(q[k]);
+            if (lane == 0) {
+                xs[gi] = sc[k];
+                xs2[gi] = s2[k];
+            }
+            if ((lane & 15) == 0) xs16[2 * gi + (lane >> 4)] = s16;
+            // (a group without a second level leaves its residual values
+            // unwritten: they enter every dot product times its s2 = 0)
+            if (s2[k] > 0.0f) {  // (warp-uniform)
+                xr[(size_t)t * cols + xq_pos(e)] = (int16_t)r[k];
+                const int r16 = sum16(r[k]);
+                if ((lane & 15) == 0) xr16[2 * gi + (lane >> 4)] = r16;
+                two = 1;
+            }
+        }
     }
+    return two;
 }
 
 // Fused greedy sampling (the argmax after the lm-head GEMV that
@@ -129,28 +186,38 @@ __device__ __forceinline__ void am_arrive(const ArgmaxArgs &am, unsigned long lo
     }
 }
 
+// One launch: the CTA quantises the activations (both levels) into shared
+// memory while its warps' first weight stages are in flight, then every warp
+// streams its rows.  A launch in which some group has a second level makes
+// two passes over its rows (the weights streamed twice): the first with the
+// first level, its row values kept in shared memory (part, `prow` rows per
+// warp), the second with the residual level, adding them -- the same loop
+// code either way, so the one-level launch runs as without outliers.
 template <int QT, int NB, bool ONE_TOKEN, bool IN_HALF, bool OUT_HALF, bool AM = false>
 __global__ void __launch_bounds__(GEMV_WARPS * 32)
 gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__restrict__ x, int T,
-                void *__restrict__ y, int rows_total, const ArgmaxArgs am)
+                void *__restrict__ y, int rows_total, long long row0, int prow, const ArgmaxArgs am)
 {
     using G = Geo<QT, NB>;
     constexpr size_t CHUNK = GemvSmem<QT, NB>::chunk;
     constexpr int GEMV_CH = GemvSmem<QT, NB>::CH;
     extern __shared__ __align__(128) uint8_t smem[];
-    const size_t o_xs = align_up((size_t)T * G::COLS * 2, 16);
-    const size_t o_xs16 = o_xs + align_up((size_t)T * G::COLS / 32 * 4, 16);
-    const size_t o_st = o_xs16 + align_up((size_t)T * G::COLS / 16 * 4, 16);
+    const GemvLayout lay(T, G::COLS);
     int16_t *xq = reinterpret_cast<int16_t *>(smem);
-    float *xs = reinterpret_cast<float *>(smem + o_xs);
-    int *xs16 = reinterpret_cast<int *>(smem + o_xs16);
-    uint8_t *stages = smem + o_st;
-    uint64_t *bars =
-        reinterpret_cast<uint64_t *>(smem + align_up(o_st + (size_t)GEMV_WARPS * GEMV_STAGES * CHUNK + 16, 8));
+    float *xs = reinterpret_cast<float *>(smem + lay.xs);
+    int *xs16 = reinterpret_cast<int *>(smem + lay.xs16);
+    int16_t *xr = reinterpret_cast<int16_t *>(smem + lay.xr);
+    float *xs2 = reinterpret_cast<float *>(smem + lay.xs2);
+    int *xr16 = reinterpret_cast<int *>(smem + lay.xr16);
+    uint8_t *stages = smem + lay.st;
+    const size_t o_bars = align_up(lay.st + (size_t)GEMV_WARPS * GEMV_STAGES * CHUNK + 16, 8);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + o_bars);
+    float *parts = reinterpret_cast<float *>(smem + align_up(o_bars + GEMV_WARPS * GEMV_STAGES * 8, 16));
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint8_t *my_stage = stages + (size_t)warp * GEMV_STAGES * CHUNK;
     uint64_t *my_bar = bars + warp * GEMV_STAGES;
+    float *part = parts + (size_t)warp * prow * T;  // [row of the warp][token]
 
     // this warp's step range
     const long long wtot = (long long)gridDim.x * GEMV_WARPS;
@@ -164,19 +231,24 @@ gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__r
         fence_mbar_init();
     }
     __syncwarp();
-    auto issue = [&](int c) {
+    // stage sequence position cc (passes one after another): weight chunk cc mod nchunks
+    auto issue = [&](int cc) {
+        const int c = cc < nchunks ? cc : cc - nchunks;
         const int first = c * GEMV_CH;
         const int n = min(GEMV_CH, nst - first);
         const unsigned bytes = (unsigned)(n * G::STEPB);
-        uint64_t *bar = my_bar + (c % GEMV_STAGES);
+        uint64_t *bar = my_bar + (cc % GEMV_STAGES);
         mbar_arrive_expect_tx(bar, bytes);
-        bulk_g2s(my_stage + (size_t)(c % GEMV_STAGES) * CHUNK, W + (s0 + first) * (long long)G::STEPB, bytes, bar);
+        bulk_g2s(my_stage + (size_t)(cc % GEMV_STAGES) * CHUNK, W + (s0 + first) * (long long)G::STEPB, bytes, bar);
     };
     if (lane == 0)
         for (int c = 0; c < min(GEMV_STAGES, nchunks); ++c) issue(c);
 
-    quantise_to_smem<IN_HALF>(x, T, G::COLS, xq, xs, xs16, warp, GEMV_WARPS, lane);
-    __syncthreads();
+    // two: some group of the launch has a second level (CTA-uniform)
+    const bool two = __syncthreads_or(
+        quantise_to_smem<IN_HALF>(x, T, G::COLS, xq, xs, xs16, xr, xs2, xr16, warp, GEMV_WARPS, lane));
+    if (two && lane == 0)
+        for (int cc = min(GEMV_STAGES, nchunks); cc < min(GEMV_STAGES, 2 * nchunks); ++cc) issue(cc);
 
     // lane geometry
     const int rho = lane / G::LPR;        // row within the warp step
@@ -188,86 +260,107 @@ gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__r
         // byte offset of this lane's block inside a 16-aligned step: 210*k, k = rho*NB + bb (+8 per pass)
         L6 = q6_lane(((rho * NB + bb) & 1) ? 2 : 0, sub & 1);
     }
-    auto slice_of = [&](XSlice &X, int t, int cp) {
+    auto slice_of = [&](XSlice &X, const int16_t *vq, const float *vs, int t, int cp) {
         const int b = cp * 8 + bb;
         if (QT == BREAD_QTYPE_Q4_K)
-            load_slice_q4k(X, xq + (size_t)t * G::COLS, xs + (size_t)t * G::COLS / 32, QK * b + 64 * sub);
+            load_slice_q4k(X, vq + (size_t)t * G::COLS, vs + (size_t)t * G::COLS / 32, QK * b + 64 * sub);
         else
-            load_slice_q6k(X, xq + (size_t)t * G::COLS, xs + (size_t)t * G::COLS / 32, QK * b + 128 * (sub >> 1),
+            load_slice_q6k(X, vq + (size_t)t * G::COLS, vs + (size_t)t * G::COLS / 32, QK * b + 128 * (sub >> 1),
                            sub & 1);
     };
-    XSlice X1[ONE_TOKEN ? G::CP : 1];
-    if (ONE_TOKEN) {
-#pragma unroll
-        for (int cp = 0; cp < G::CP; ++cp) slice_of(X1[cp], 0, cp);
-    }
 
     unsigned long long best = 0ull;  // AM: this lane's best key
-    for (int c = 0; c < nchunks; ++c) {
-        const int slot = c % GEMV_STAGES;
-        if (!mbar_wait(my_bar + slot, (unsigned)((c / GEMV_STAGES) & 1))) return;
-        const uint8_t *buf = my_stage + (size_t)slot * CHUNK;
-        const int n = min(GEMV_CH, nst - c * GEMV_CH);
-        for (int st = 0; st < n; ++st) {
-            const long long row = (s0 + c * GEMV_CH + st) * G::RPW + rho;
-            const uint8_t *rowp = buf + (size_t)st * G::STEPB + (size_t)rho * G::ROWB;
-            float acc[ONE_TOKEN ? 1 : GEMV_TMAX];
+    // The row loop over one activation level.  MODE 0: the only pass (writes
+    // the outputs); 1: first of two passes (keeps the row values); 2: second
+    // of two (adds the kept values, writes the outputs).  cc0: stage sequence
+    // position of the pass's first chunk.
+    auto rows = [&](auto mode_c, const int16_t *vq, const float *vs, const int *v16, int cc0) -> bool {
+        constexpr int MODE = decltype(mode_c)::value;
+        XSlice X1[ONE_TOKEN ? G::CP : 1];
+        if (ONE_TOKEN) {
 #pragma unroll
-            for (int t = 0; t < (ONE_TOKEN ? 1 : GEMV_TMAX); ++t) acc[t] = 0.0f;
+            for (int cp = 0; cp < G::CP; ++cp) slice_of(X1[cp], vq, vs, 0, cp);
+        }
+        for (int c = 0; c < nchunks; ++c) {
+            const int cc = MODE == 2 ? c + cc0 : c;
+            const int slot = cc % GEMV_STAGES;
+            if (!mbar_wait(my_bar + slot, (unsigned)((cc / GEMV_STAGES) & 1))) return false;
+            const uint8_t *buf = my_stage + (size_t)slot * CHUNK;
+            const int n = min(GEMV_CH, nst - c * GEMV_CH);
+            for (int st = 0; st < n; ++st) {
+                const int rw = (c * GEMV_CH + st) * G::RPW + rho;  // row within the warp's range
+                const long long row = row0 + s0 * G::RPW + rw;
+                const uint8_t *rowp = buf + (size_t)st * G::STEPB + (size_t)rho * G::ROWB;
+                float acc[ONE_TOKEN ? 1 : GEMV_TMAX];
 #pragma unroll
-            for (int cp = 0; cp < G::CP; ++cp) {
-                const uint8_t *blk = rowp + (size_t)(cp * 8 + bb) * G::BB;
-                if (ONE_TOKEN) {
-                    acc[0] += QT == BREAD_QTYPE_Q4_K ? q4k_lane_dot(blk, sub, X1[cp])
-                                                     : q6k_lane_dot(blk, sub >> 1, sub & 1, L6, X1[cp]);
-                } else if (QT == BREAD_QTYPE_Q4_K) {
-                    // several tokens: decode the lane's weights once, then one
-                    // dot per token from its slice in shared memory
-                    Q4W W;
-                    q4k_lane_w(W, blk, sub);
-                    const int e0 = QK * (cp * 8 + bb) + 64 * sub;
+                for (int t = 0; t < (ONE_TOKEN ? 1 : GEMV_TMAX); ++t) acc[t] = 0.0f;
 #pragma unroll
-                    for (int t = 0; t < GEMV_TMAX; ++t)
-                        if (t < T)
-                            acc[t] += q4k_dot_w(W, xq + (size_t)t * G::COLS, xs + (size_t)t * G::COLS / 32,
-                                                xs16 + (size_t)t * G::COLS / 16, e0, 1.0f);
-                } else {
-                    Q6W W;
-                    q6k_lane_w(W, blk, sub >> 1, sub & 1, L6);
-                    const int base = QK * (cp * 8 + bb) + 128 * (sub >> 1);
+                for (int cp = 0; cp < G::CP; ++cp) {
+                    const uint8_t *blk = rowp + (size_t)(cp * 8 + bb) * G::BB;
+                    if (ONE_TOKEN) {
+                        acc[0] += QT == BREAD_QTYPE_Q4_K ? q4k_lane_dot(blk, sub, X1[cp])
+                                                         : q6k_lane_dot(blk, sub >> 1, sub & 1, L6, X1[cp]);
+                    } else if (QT == BREAD_QTYPE_Q4_K) {
+                        // several tokens: decode the lane's weights once, then one
+                        // dot per token from its slice in shared memory
+                        Q4W Wd;
+                        q4k_lane_w(Wd, blk, sub);
+                        const int e0 = QK * (cp * 8 + bb) + 64 * sub;
 #pragma unroll
-                    for (int t = 0; t < GEMV_TMAX; ++t)
-                        if (t < T)
-                            acc[t] += q6k_dot_w(W, xq + (size_t)t * G::COLS, xs + (size_t)t * G::COLS / 32,
-                                                xs16 + (size_t)t * G::COLS / 16, base, sub & 1, 1.0f);
+                        for (int t = 0; t < GEMV_TMAX; ++t)
+                            if (t < T)
+                                acc[t] += q4k_dot_w(Wd, vq + (size_t)t * G::COLS, vs + (size_t)t * G::COLS / 32,
+                                                    v16 + (size_t)t * G::COLS / 16, e0, 1.0f);
+                    } else {
+                        Q6W Wd;
+                        q6k_lane_w(Wd, blk, sub >> 1, sub & 1, L6);
+                        const int base = QK * (cp * 8 + bb) + 128 * (sub >> 1);
+#pragma unroll
+                        for (int t = 0; t < GEMV_TMAX; ++t)
+                            if (t < T)
+                                acc[t] += q6k_dot_w(Wd, vq + (size_t)t * G::COLS, vs + (size_t)t * G::COLS / 32,
+                                                    v16 + (size_t)t * G::COLS / 16, base, sub & 1, 1.0f);
+                    }
                 }
-            }
 #pragma unroll
-            for (int t = 0; t < (ONE_TOKEN ? 1 : GEMV_TMAX); ++t) {
-                if (ONE_TOKEN || t < T) {
-                    float v = acc[t];
+                for (int t = 0; t < (ONE_TOKEN ? 1 : GEMV_TMAX); ++t) {
+                    if (ONE_TOKEN || t < T) {
+                        float v = acc[t];
 #pragma unroll
-                    for (int o = G::LPR / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                    if (lr == 0) {
-                        const size_t oi = (size_t)t * rows_total + row;
-                        if (AM) {
-                            const unsigned long long k = am_key(v, row, am.round_half);
-                            best = k > best ? k : best;
-                            if (y) reinterpret_cast<float *>(y)[oi] = v;
-                        } else if (OUT_HALF) {
-                            reinterpret_cast<__half *>(y)[oi] = __float2half_rn(v);
-                        } else {
-                            reinterpret_cast<float *>(y)[oi] = v;
+                        for (int o = G::LPR / 2; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                        if (lr == 0) {
+                            if (MODE == 1) {
+                                part[(size_t)rw * T + t] = v;
+                                continue;
+                            }
+                            if (MODE == 2) v += part[(size_t)rw * T + t];
+                            const size_t oi = (size_t)t * rows_total + row;
+                            if (AM) {
+                                const unsigned long long k = am_key(v, row, am.round_half);
+                                best = k > best ? k : best;
+                                if (y) reinterpret_cast<float *>(y)[oi] = v;
+                            } else if (OUT_HALF) {
+                                reinterpret_cast<__half *>(y)[oi] = __float2half_rn(v);
+                            } else {
+                                reinterpret_cast<float *>(y)[oi] = v;
+                            }
                         }
                     }
                 }
             }
+            __syncwarp();
+            if (lane == 0 && cc + GEMV_STAGES < (MODE == 0 ? nchunks : 2 * nchunks)) {
+                fence_proxy_async_smem();
+                issue(cc + GEMV_STAGES);
+            }
         }
-        __syncwarp();
-        if (lane == 0 && c + GEMV_STAGES < nchunks) {
-            fence_proxy_async_smem();
-            issue(c + GEMV_STAGES);
-        }
+        return true;
+    };
+    if (!two) {
+        if (!rows(std::integral_constant<int, 0>{}, xq, xs, xs16, 0)) return;
+    } else {
+        if (!rows(std::integral_constant<int, 1>{}, xq, xs, xs16, 0)) return;
+        if (!rows(std::integral_constant<int, 2>{}, xr, xs2, xr16, nchunks)) return;
     }
     if (AM) am_arrive(am, best, gridDim.x * GEMV_WARPS);
 }
@@ -331,28 +424,50 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ W, float *__restrict_
 // ---------------------------------------------------------------------------
 // host dispatch
 // ---------------------------------------------------------------------------
+constexpr size_t GEMV_SMEM_MAX = 232448;  // dynamic shared memory per CTA (227 KB)
+
+// One matrix, in pieces of rows when the two-pass row values of a piece
+// would not fit in shared memory (only for very tall matrices); with AM only
+// the last piece finalises.
 template <int QT, int NB, bool ONE, bool IH, bool OH, bool AM = false>
 static int launch_fast(const uint8_t *W, long long nsteps, const void *x, int T, void *y, int rows_total,
                        cudaStream_t stream, const ArgmaxArgs &am = ArgmaxArgs{})
 {
+    using G = Geo<QT, NB>;
     auto kern = gemv_tma_kernel<QT, NB, ONE, IH, OH, AM>;
-    const size_t smem = GemvSmem<QT, NB>::bytes(T);
-    static int per_sm = 0;  // per instantiation; the attribute covers the largest T
+    if (T > (ONE ? 1 : gemv_tmax(NB))) return set_error(BREAD_ERR_ARG, "gemv: %d tokens in one launch at %d columns", T, NB * QK);
+    static int per_sm = 0;  // per instantiation: CTAs per SM without the row values
     if (!per_sm) {
-        BREAD_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)GemvSmem<QT, NB>::bytes(ONE ? 1 : GEMV_TMAX)),
+        BREAD_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMV_SMEM_MAX),
                    "gemv: set smem attribute");
         int n = 1;
         BREAD_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, GEMV_WARPS * 32,
-                                                                 GemvSmem<QT, NB>::bytes(ONE ? 1 : GEMV_TMAX)),
+                                                                 GemvSmem<QT, NB>::bytes(ONE ? 1 : gemv_tmax(NB), 0)),
                    "gemv occupancy");
         per_sm = n < 1 ? 1 : n;
     }
-    const long long want = (nsteps + GEMV_WARPS - 1) / GEMV_WARPS;
+    const size_t base = GemvSmem<QT, NB>::bytes(T, 0) + 16;
+    const long long steps_fit = base < GEMV_SMEM_MAX ? (long long)((GEMV_SMEM_MAX - base) / ((size_t)GEMV_WARPS * T * 4)) / G::RPW : 0;
+    if (steps_fit < 1) return set_error(BREAD_ERR_ARG, "gemv: %d tokens at %d columns exceed shared memory", T, NB * QK);
     const long long cap = (long long)sm_count() * per_sm;
-    const int grid = (int)(want < cap ? want : cap);
-    kern<<<grid, GEMV_WARPS * 32, smem, stream>>>(W, nsteps, x, T, y, rows_total, am);
-    BREAD_CUDA(cudaGetLastError(), "gemv fast launch");
+    for (long long done = 0; done < nsteps;) {
+        long long ns = nsteps - done;
+        const long long want = (ns + GEMV_WARPS - 1) / GEMV_WARPS;
+        const int grid = (int)(want < cap ? want : cap);
+        const long long wtot = (long long)grid * GEMV_WARPS;
+        long long per_warp = (ns + wtot - 1) / wtot;  // steps of the busiest warp
+        if (per_warp > steps_fit) {
+            per_warp = steps_fit;
+            ns = per_warp * wtot;
+        }
+        ArgmaxArgs piece = am;
+        if (done + ns < nsteps) piece.finalize = 0;
+        const int prow = (int)(per_warp * G::RPW);
+        kern<<<grid, GEMV_WARPS * 32, GemvSmem<QT, NB>::bytes(T, prow), stream>>>(
+            W + done * G::STEPB, ns, x, T, y, rows_total, done * G::RPW, prow, piece);
+        BREAD_CUDA(cudaGetLastError(), "gemv fast launch");
+        done += ns;
+    }
     return BREAD_OK;
 }
 
@@ -456,9 +571,10 @@ extern "C" int bread_matvec_batch_f32(const void *w, const float *x, float *y, i
                                       cudaStream_t stream)
 {
     BREAD_TRY(check_gemv_args(w, x, y, rows, cols, qtype, T));
-    // token chunks of GEMV_TMAX: each chunk streams the weights once
-    for (int t0 = 0; t0 < T; t0 += GEMV_TMAX) {
-        const int n = T - t0 < GEMV_TMAX ? T - t0 : GEMV_TMAX;
+    // token chunks (8, or 4 at 4096 columns): each chunk streams the weights once
+    const int tc = gemv_tmax(cols / QK);
+    for (int t0 = 0; t0 < T; t0 += tc) {
+        const int n = T - t0 < tc ? T - t0 : tc;
         BREAD_TRY(gemv_any<false, false>(w, qtype, rows, cols, x + (size_t)t0 * cols, n, y + (size_t)t0 * rows,
                                          stream));
     }

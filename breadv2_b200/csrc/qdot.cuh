@@ -11,7 +11,9 @@
 //         sum_i w_i x_i = d*sc*s_x*SUM(q_i xq_i) - dmin*m*s_x*SUM(xq_i)
 //     where xq_i = round(x_i / s_x) and the inner SUMs are exact int32 dot
 //     products (dp2a).  The only approximation is x ~= s_x*xq
-//     (|error| <= s_x/2 = max|x_group| / 65534).
+//     (|error| <= s_x/2 = max|x_group| / 65534); the GEMV adds a second
+//     int16 level for groups with outliers (quant32_r_n), taking the error of
+//     those groups to max|x_group| / 2^31.
 #pragma once
 #include <stdint.h>
 #include "common.cuh"
@@ -96,6 +98,63 @@ __device__ __forceinline__ int quant32(float v, float *scale, int lane)
     if (a > 0.0f && finite) q = __float2int_rn((v / a) * 32767.0f);  // |v/a| <= 1, also for subnormal a
     if (lane == 0) *scale = finite ? a * (1.0f / 32767.0f) : __int_as_float(0x7fc00000);
     return q;
+}
+
+// quant32 with a second level for a group whose largest value dwarfs the
+// rest (outliers, e.g. a massive-activation channel): r quantises the first
+// level's error v - q*s to int16 with scale s2, so v ~= q*s + r*s2 with an
+// error below s2/2 = max|v| / 2^31.  The first level's rounding error (up to
+// s/2, s = max|v|/32767) costs a dot product a relative ~ s / (sqrt(12) *
+// rms) of the values it weights; when the weights skip the large values,
+// rms is that of the rest.  So a group keeps the second level (s2 > 0) when
+// max|v| > 16 * rms of its values below 0.35 max|v| -- where one level would
+// cost more than ~1.4e-4 -- which normal or Laplace data meets in ~1e-5 of
+// its groups.  Otherwise r = 0, s2 = 0 and q, s are exactly quant32's.
+// N groups at once (one value of each per lane, reductions interleaved);
+// q, r, s, s2 of group k valid on every lane.
+template <int N>
+__device__ __forceinline__ void quant32_r_n(const float (&v)[N], int (&q)[N], int (&r)[N], float (&s)[N],
+                                            float (&s2)[N])
+{
+    float a[N], sm[N];
+    bool finite[N];
+    int n[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+        a[k] = fabsf(v[k]);
+        finite[k] = !__any_sync(0xffffffffu, !(a[k] <= 3.402823466e38f));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+#pragma unroll
+        for (int k = 0; k < N; ++k) a[k] = fmaxf(a[k], __shfl_xor_sync(0xffffffffu, a[k], o));
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+        q[k] = (a[k] > 0.0f && finite[k]) ? __float2int_rn((v[k] / a[k]) * 32767.0f) : 0;
+        s[k] = finite[k] ? a[k] * (1.0f / 32767.0f) : __int_as_float(0x7fc00000);
+        const bool rest = fabsf(v[k]) < 0.35f * a[k];
+        n[k] = __popc(__ballot_sync(0xffffffffu, rest));
+        sm[k] = rest ? v[k] * v[k] : 0.0f;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+#pragma unroll
+        for (int k = 0; k < N; ++k) sm[k] += __shfl_xor_sync(0xffffffffu, sm[k], o);
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+        r[k] = 0;
+        s2[k] = 0.0f;
+        if (finite[k] && a[k] > 0.0f && a[k] * a[k] * (float)n[k] > 256.0f * sm[k]) {  // (warp-uniform)
+            const float e = fmaf(-(float)q[k], s[k], v[k]);
+            float b = fabsf(e);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, o));
+            if (b > 0.0f) {
+                r[k] = __float2int_rn((e / b) * 32767.0f);
+                s2[k] = b * (1.0f / 32767.0f);
+            }
+        }
+    }
 }
 
 // N groups at once (one value of each per lane), the same arithmetic per

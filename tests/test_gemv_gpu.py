@@ -71,6 +71,58 @@ def test_matvec_activation_edges(cuda, orc, qt):
     assert np.all(np.isnan(yn))
 
 
+def _zero_column(w, qt, rows, cols, c):
+    """Give column c zero weight in every row, keeping the other columns of
+    its 32-value group: Q4_K with dmin = 0 and that element's nibble 0;
+    Q6_K with that element's 6-bit value 32 (dequant_q4k_cpu.c:146-172)."""
+    blk = w.reshape(rows, cols // 256, -1)
+    b, e = divmod(c, 256)
+    if qt == 12:
+        blk[:, b, 2:4] = 0
+        g, within = divmod(e, 64)
+        i = 16 + 32 * g + within % 32
+        blk[:, b, i] &= np.uint8(0xF0 if within < 32 else 0x0F)
+    else:
+        h, e2 = divmod(e, 128)
+        r, l = divmod(e2, 32)
+        i = 64 * h + l + 32 * (r & 1)
+        blk[:, b, i] &= np.uint8(0xF0 if r < 2 else 0x0F)
+        j = 128 + 32 * h + l
+        blk[:, b, j] = (blk[:, b, j] & np.uint8(0xFF ^ (3 << (2 * r)))) | np.uint8(2 << (2 * r))
+
+
+@pytest.mark.parametrize("qt", [12, 14])
+@pytest.mark.parametrize("T,cols", [(1, 2048), (3, 2048), (1, 4096), (6, 4096), (8, 512)])
+def test_matvec_outlier_groups(cuda, orc, qt, T, cols):
+    """Massive activations (3e4, -2e4 among N(0,1) values) in two columns of
+    one 32-value group, which every row weights by zero: the output is made
+    of the other values only -- the 30 that share the outliers' quantisation
+    group included -- so their precision is what the check sees.  (One int16
+    level per group would leave those 30 values ~5 bits; the group's second
+    level restores them.)  Plus a group of tiny values in the last token."""
+    rng = np.random.default_rng(41 + qt + 10 * T + cols)
+    rows = 256
+    w = B.matrix(qt, rng, rows, cols)
+    c1, c2 = 32 * 5 + 17, 32 * 5 + 3
+    _zero_column(w, qt, rows, cols, c1)
+    _zero_column(w, qt, rows, cols, c2)
+    wf = orc.dequant(w, qt, rows * cols // 256).reshape(rows, cols)
+    assert np.all(wf[:, [c1, c2]] == 0) and np.count_nonzero(wf[:, 32 * 5:32 * 6]) > rows * 20
+    x = rng.standard_normal((T, cols)).astype(np.float32)
+    x[:, c1] = 3e4
+    x[:, c2] = -2e4
+    x[-1, 64:96] = 1e-30
+    y = bb.matvec_f32(dev(w, cuda), dev(x[0] if T == 1 else x, cuda), rows, cols, qt).cpu().numpy().reshape(T, rows)
+    ref = orc.matvec_f64(w, qt, x, rows, cols).reshape(T, rows)
+    for t in range(T):
+        assert orc.rel_l2(y[t], ref[t]) < TOL
+    # the fp16 drop-in (fp16 x and y): within its output rounding
+    xh = x[0].astype(np.float16)
+    yh = torch.empty(rows, dtype=torch.float16, device=cuda)
+    bb.matvec(dev(w, cuda), dev(xh, cuda), yh, rows, cols, qt)
+    assert orc.rel_l2(yh.float().cpu().numpy(), orc.matvec_f64(w, qt, xh.astype(np.float32), rows, cols)) < 2e-3
+
+
 @pytest.mark.parametrize("qt,rows,cols", [(12, 512, 2048), (14, 2048, 512), (12, 33, 512)])
 def test_matvec_unaligned_weights(cuda, orc, qt, rows, cols):
     """Weights at a 2-byte offset take the alignment-agnostic path."""
