@@ -792,6 +792,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="profiler runs: timed steps only (no load phase, end-to-end pass, kernel events or CPU baseline)")
+    ap.add_argument("--gemv", action="store_true",
+                    help="profiler runs: only the output-head GEMV measurement (Q6_K then Q4_K, 3 + 10 launches each)")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -801,6 +803,13 @@ def main(argv=None) -> int:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.gemv:
+        import torch
+
+        dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(dev)
+        print(json.dumps({"matvec": matvec_bench(dev, peaks()[0])}), flush=True)
+        return 0
     return run_ours(args, rank, world, local_rank)
 
 
