@@ -42,7 +42,10 @@ struct Geo {
 };
 
 constexpr int GEMV_WARPS = 8;
-constexpr int GEMV_STAGES = 3;   // shared-memory stages per warp
+// shared-memory stages per warp: two for one token at 2048 columns (2 x 8 x
+// 3.4 KB, so three CTAs fit an SM: 24 warps hide the decode latency better
+// than a third stage does), three otherwise
+__host__ __device__ constexpr int gemv_stages(int nb, bool one) { return one && nb == 8 ? 2 : 3; }
 constexpr int GEMV_TMAX = 8;     // tokens per launch on the fast path
 // tokens per launch at NB super-blocks per row: at 4096 columns eight tokens'
 // two activation levels would not fit in shared memory beside the stages
@@ -82,8 +85,9 @@ struct GemvSmem {
     static size_t bytes(int T, int prow)
     {
         size_t b = GemvLayout(T, Geo<QT, NB>::COLS).st;
-        b += (size_t)GEMV_WARPS * GEMV_STAGES * chunk + 16;                    // stages + tail pad
-        b = align_up(b, 8) + GEMV_WARPS * GEMV_STAGES * 8;                     // mbarriers
+        const int ns = gemv_stages(NB, T == 1);
+        b += (size_t)GEMV_WARPS * ns * chunk + 16;                             // stages + tail pad
+        b = align_up(b, 8) + GEMV_WARPS * ns * 8;                              // mbarriers
         b = align_up(b, 16) + (size_t)GEMV_WARPS * prow * T * 4;               // row values
         return b;
     }
@@ -194,13 +198,14 @@ __device__ __forceinline__ void am_arrive(const ArgmaxArgs &am, unsigned long lo
 // warp), the second with the residual level, adding them -- the same loop
 // code either way, so the one-level launch runs as without outliers.
 template <int QT, int NB, bool ONE_TOKEN, bool IN_HALF, bool OUT_HALF, bool AM = false>
-__global__ void __launch_bounds__(GEMV_WARPS * 32)
+__global__ void __launch_bounds__(GEMV_WARPS * 32, ONE_TOKEN && NB == 8 ? 3 : 1)
 gemv_tma_kernel(const uint8_t *__restrict__ W, long long nsteps, const void *__restrict__ x, int T,
                 void *__restrict__ y, int rows_total, long long row0, int prow, const ArgmaxArgs am)
 {
     using G = Geo<QT, NB>;
     constexpr size_t CHUNK = GemvSmem<QT, NB>::chunk;
     constexpr int GEMV_CH = GemvSmem<QT, NB>::CH;
+    constexpr int GEMV_STAGES = gemv_stages(NB, ONE_TOKEN);
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvLayout lay(T, G::COLS);
     int16_t *xq = reinterpret_cast<int16_t *>(smem);
