@@ -68,13 +68,17 @@ def layer_timeline(stamps) -> dict:
     24] (ns): median and max over CTAs of each phase point, in us from the
     earliest start of the layer, averaged over layers.  A point a CTA never
     reaches (no work of that kind) stays 0 and is left out of the median."""
+    import warnings
+
     import numpy as np
 
     s = stamps.astype(np.float64)
     st0 = s[:, :, 0].min(axis=1)[:, None, None]
     rel = np.where(s > 0, (s - st0) * 1e-3, np.nan)
-    med = np.nanmean(np.nanmedian(rel, axis=1), axis=0)
-    mx = np.nanmean(np.nanmax(rel, axis=1), axis=0)
+    with warnings.catch_warnings():  # (points no CTA reaches in some mode are NaN)
+        warnings.simplefilter("ignore", RuntimeWarning)
+        med = np.nanmean(np.nanmedian(rel, axis=1), axis=0)
+        mx = np.nanmean(np.nanmax(rel, axis=1), axis=0)
     return {"points": STAMP_POINTS, "median_us": [round(float(v), 2) for v in med],
             "max_us": [round(float(v), 2) for v in mx]}
 
