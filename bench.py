@@ -79,8 +79,10 @@ def layer_timeline(stamps) -> dict:
         warnings.simplefilter("ignore", RuntimeWarning)
         med = np.nanmean(np.nanmedian(rel, axis=1), axis=0)
         mx = np.nanmean(np.nanmax(rel, axis=1), axis=0)
-    return {"points": STAMP_POINTS, "median_us": [round(float(v), 2) for v in med],
-            "max_us": [round(float(v), 2) for v in mx]}
+    def r2(v):  # (strict JSON: a point no CTA reached is null)
+        return round(float(v), 2) if v == v else None
+
+    return {"points": STAMP_POINTS, "median_us": [r2(v) for v in med], "max_us": [r2(v) for v in mx]}
 
 
 class ClockSampler:
