@@ -393,8 +393,9 @@ __device__ __forceinline__ ChunkInfo chunk_search(const RouteTabs &R, int c)
 struct NoEarly {
     __device__ void operator()(int) const {}
 };
-// `early(e)` runs (all lanes) as soon as pick number `kw` is known.
-template <int PER, bool LLM = false, class Early = NoEarly>
+// `early(e)` runs (all lanes) as soon as pick number `kw` is known; with
+// EVERY, `early(k, e)` runs at every pick k instead.
+template <int PER, bool LLM = false, class Early = NoEarly, bool EVERY = false>
 __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *idx, float *w, float *rinv,
                             float *sgw, bool outputs, unsigned long long *st, int l, int *pick_i = nullptr,
                             float *pick_w = nullptr, float *pick_sg = nullptr,
@@ -455,7 +456,10 @@ __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *
         for (int j = PER - 1; j >= 0; --j)
             if (key[j] == mk) cand = (unsigned)(lane + 32 * j);
         const unsigned bi = __reduce_min_sync(0xffffffffu, cand);
-        if (k == kw) early((int)bi);
+        if constexpr (EVERY)
+            early(k, (int)bi);
+        else if (k == kw)
+            early((int)bi);
         if ((int)(bi & 31) == lane) {
 #pragma unroll
             for (int j = 0; j < PER; ++j)
@@ -502,7 +506,7 @@ __device__ void route_token(const StepArgs &a, const StepLayer &Ld, int t, int *
 // routed experts held here, pairs token-major inside each group.
 // LLM: the logits come as flagged words (llg, tag) and, before anything else,
 // warp 0 waits for the presence word of every CTA for this layer (pres).
-template <int PER, bool BIG, bool LLM = false, bool T1 = false, class Early = NoEarly>
+template <int PER, bool BIG, bool LLM = false, bool T1 = false, class Early = NoEarly, bool EVERY = false>
 __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const RouteTabs &R, int l, bool cta0,
                              unsigned long long *st, bool dist, const unsigned long long *llg = nullptr,
                              const unsigned long long *pres = nullptr, const float *ssq_l = nullptr,
@@ -542,7 +546,7 @@ __device__ void route_tables(const StepArgs &a, const StepLayer &Ld, const Route
         if (warp == 0) {
             int e;
             float w, sg;
-            route_token<PER, LLM, Early>(a, Ld, 0, R.idx, R.w, R.rinv, R.sgw, cta0, (st && lane == 0) ? st : nullptr,
+            route_token<PER, LLM, Early, EVERY>(a, Ld, 0, R.idx, R.w, R.rinv, R.sgw, cta0, (st && lane == 0) ? st : nullptr,
                                          l, &e, &w, &sg, llg, ssq_l, tag, kw, early);
             const int hs = Ld.sh_gate ? 1 : 0;
             const bool loc = lane < K && e >= a.lo && e < a.hi;
@@ -1454,7 +1458,41 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
             const unsigned long long *llg = LL ? a.ll_lg + par_of(l) * a.ll_lg_n : nullptr;
             const unsigned long long *pres =
                 (LL && E + (Ld.w_sg ? 1 : 0) < G) ? a.ll_pres + par_of(l) * a.ll_pres_n : nullptr;
-            if constexpr (T1) {
+            if constexpr (T1 && MODE == MODE_LLEP) {
+                // One token with expert parallelism: the same early request
+                // as below, but a rank's chunks are its own picks in top-k
+                // order, so the routing warp counts the local picks as they
+                // come and requests this CTA's item at the local pick of its
+                // chunk.
+                const int hs = Ld.sh_gate ? 1 : 0, c0 = bx / R;
+                const int kw = (Ld.gate_base && c0 >= hs && c0 < hs + a.top_k) ? c0 - hs : -1;
+                if (warp == 0 && lane == 0) RT.scal[3] = 0;
+                int nloc = 0;  // local picks so far (the same on every lane)
+                auto early = [&](int, int e) {
+                    if (e < a.lo || e >= a.hi) return;
+                    if (nloc++ != kw) return;
+                    const int n = C::SPI < NS_G ? C::SPI : NS_G;
+                    const size_t j = (size_t)(e - a.lo);
+                    const uint8_t *gb = Ld.gate_base + j * Ld.gu_stride, *ub = Ld.up_base + j * Ld.gu_stride;
+                    if (lane < n) {
+                        const Ring g = gR.ahead(lane, NS_G);
+                        const unsigned bytes = (unsigned)(C::SR * GH::ROWB);
+                        const size_t r0 = (size_t)(bx % R) * MOE_ROWTILE + (size_t)lane * C::SR;
+                        uint8_t *dst = gring + (size_t)g.slot * C::STB;
+                        if (!((reinterpret_cast<uintptr_t>(gb) | reinterpret_cast<uintptr_t>(ub)) & 15)) {
+                            mbar_arrive_expect_tx(gfull + g.slot, 2 * bytes);
+                            bulk_g2s(dst, gb + r0 * GH::ROWB, bytes, gfull + g.slot);
+                            bulk_g2s(dst + bytes, ub + r0 * GH::ROWB, bytes, gfull + g.slot);
+                        } else {
+                            flag_error(DEVERR_ROUTE);
+                            mbar_arrive(gfull + g.slot);
+                        }
+                    }
+                    if (lane == 0) RT.scal[3] = n;
+                };
+                route_tables<8, BIG, LL, T1, decltype(early), true>(a, Ld, RT, l, bx == 0, st_l, dist, llg, pres, ssql,
+                                                                    tg, -1, early);
+            } else if constexpr (T1) {
                 // One token: the routing warp requests this CTA's first gate/up
                 // item itself as soon as the item's expert is picked (pick
                 // bx / R - shared, in top-k order: the order of the chunks),
@@ -1463,8 +1501,8 @@ __global__ void __launch_bounds__(ST_THREADS, 1) moe_step_kernel(const __grid_co
                 // in the last layer's item loop, which every consumer warp has
                 // left), and tells the producer how many sub-stages to skip.
                 const int hs = Ld.sh_gate ? 1 : 0, c0 = bx / R;
-                // (one GPU only: with expert parallelism the chunks follow the
-                // rank's own picks, not the top-k order)
+                // (one GPU: with expert parallelism the chunks follow the
+                // rank's own picks -- the instantiation above)
                 const int kw = (Ld.gate_base && a.ep_world == 1 && c0 >= hs && c0 < hs + a.top_k) ? c0 - hs : -1;
                 if (warp == 0 && lane == 0) RT.scal[3] = 0;
                 auto early = [&](int e) {
